@@ -1,0 +1,110 @@
+"""CPU tests of the C-ABI boundary: the library loads without a GPU, exports
+every function the header declares, and the ctypes struct matches the C layout."""
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+
+import pytest
+
+import oracle
+from paged_attention import _native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "pa_decode.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    return re.findall(r"PA_API\s+[\w\s\*]+?\b(pa_\w+)\s*\(", text)
+
+
+def test_header_declares_expected_entry_points():
+    names = set(_declared_functions())
+    assert {"pa_decode", "pa_decode_workspace", "pa_num_splits_heuristic", "pa_stream_copy",
+            "pa_stream_read", "pa_device_sm_count", "pa_status_string",
+            "pa_abi_version"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    for name in _declared_functions():
+        assert hasattr(lib, name), f"{name} not exported by {_native.library_path()}"
+    assert lib.pa_abi_version() == 1
+
+
+def test_library_has_no_cudart_runtime_dependency():
+    ldd = shutil.which("ldd")
+    if not ldd:
+        pytest.skip("ldd not available")
+    out = subprocess.run([ldd, _native.library_path()], capture_output=True, text=True).stdout
+    assert "libcudart" not in out and "libcuda.so" not in out
+
+
+def test_struct_layout_matches_header(tmp_path):
+    gcc = shutil.which("gcc")
+    if not gcc:
+        pytest.skip("gcc not available")
+    fields = [f[0] for f in _native.DecodeParams._fields_]
+    src = ['#include <stdio.h>', '#include <stddef.h>', '#include "pa_decode.h"',
+           'int main(void) {', 'printf("size %zu\\n", sizeof(pa_decode_params));']
+    for f in fields:
+        src.append(f'printf("{f} %zu\\n", offsetof(pa_decode_params, {f}));')
+    src += ["return 0;", "}"]
+    c = tmp_path / "probe.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "probe"
+    cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+    subprocess.run([gcc, "-I", os.path.join(ROOT, "include"), "-I", cuda_inc, str(c), "-o",
+                    str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
+    got = dict(line.split() for line in out.strip().splitlines())
+    assert int(got["size"]) == ctypes.sizeof(_native.DecodeParams)
+    for f in fields:
+        assert int(got[f]) == getattr(_native.DecodeParams, f).offset, f
+
+
+@pytest.mark.parametrize("b,h,s,bs,sm", [(1, 32, 128, 16, 148), (32, 32, 1024, 16, 148),
+                                         (1, 32, 4096, 128, 148), (128, 32, 256, 16, 148),
+                                         (1, 8, 4096, 16, 20), (3, 5, 7, 8, 1), (1, 1, 0, 16, 148)])
+def test_heuristic_matches_reference_formula(b, h, s, bs, sm):
+    assert _native.lib().pa_num_splits_heuristic(b, h, s, bs, sm) == \
+        oracle.num_splits_heuristic(b, h, s, bs, sm)
+
+
+def _params(**kw):
+    p = _native.DecodeParams()
+    p.batch, p.num_heads, p.num_kv_heads, p.head_dim = 2, 8, 2, 128
+    p.block_size, p.num_blocks, p.max_blocks, p.seq_len = 16, 8, 4, 50
+    p.scale, p.dtype = 0.088, _native.PA_F16
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize("kw,code", [
+    ({"num_heads": 6, "num_kv_heads": 4}, _native.PA_ERR_ARG),     # Hq % Hkv != 0
+    ({"dtype": 7}, _native.PA_ERR_ARG),
+    ({"seq_len": 65}, _native.PA_ERR_ARG),                          # > max_blocks * bs
+    ({"num_splits": -1}, _native.PA_ERR_ARG),
+    ({"head_dim": 64}, _native.PA_ERR_UNSUPPORTED),
+    ({"block_size": 12, "seq_len": 40}, _native.PA_ERR_UNSUPPORTED),
+])
+def test_host_validation_without_gpu(kw, code):
+    lib = _native.lib()
+    p = _params(**kw)
+    a, b = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert lib.pa_decode_workspace(ctypes.byref(p), ctypes.byref(a), ctypes.byref(b)) == code
+    assert lib.pa_decode(ctypes.byref(p), None) == code
+
+
+def test_null_params_rejected():
+    lib = _native.lib()
+    assert lib.pa_decode(None, None) == _native.PA_ERR_ARG
+    assert lib.pa_stream_copy(None, None, 16, None) == _native.PA_ERR_ARG
+
+
+def test_status_strings():
+    assert _native.status_string(0) == "ok"
+    assert "unsupported" in _native.status_string(2)
