@@ -32,7 +32,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -78,60 +77,122 @@ def _profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling (200 ms) during the timed region."""
+    """SM clock and throttle-reason sampling during the timed region.
+
+    Polls NVML every 10 ms from a thread (read-only queries); falls back to
+    ``nvidia-smi -lms 200`` when NVML is unavailable."""
+
+    # NVML clocks-event reason bits
+    _REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
-        self.proc = None
-        self.thread = None
+        self.samples = []       # (sm_mhz, reason_bits)
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
 
     def __enter__(self):
-        cmd = ["nvidia-smi", "-i", str(self.index),
-               "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-               "--format=csv,noheader,nounits", "-lms", "200"]
         try:
-            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
-        except OSError:
-            self.proc = None
-            return self
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
 
-        def reader():
-            for line in self.proc.stdout:
-                self.samples.append([x.strip() for x in line.split(",")])
-        self.thread = threading.Thread(target=reader, daemon=True)
-        self.thread.start()
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, bits))
+                    except Exception:
+                        pass
+                    self._stop.wait(0.01)
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
+            t0 = time.time()
+            while not self.samples and time.time() - t0 < 1.0:
+                time.sleep(0.005)
+        except Exception:
+            self._thread = None
         return self
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+    def _physical_index(self):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+                return int(vis.split(",")[self.index])
+            except (ValueError, IndexError):
+                pass
+        return self.index
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        rows = [s for s in self.samples if len(s) >= 8]
+        rows = list(self.samples)
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"],
+                    "samples": 0}
+        reasons = sorted({name for _, bits in rows for bit, name in self._REASONS.items()
+                          if bits & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in rows), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(rows), "source": "nvml 10 ms"}
 
 
 def _stats(ms):
     return {"mean": statistics.fmean(ms), "median": statistics.median(ms), "min": min(ms),
             "max": max(ms)}
+
+
+# ----------------------------------------------------------------------------- ranks
+SEEDS = {"c1": 1, "c2": 2, "c3": 3, "c4": 4, "c5": 5}
+
+
+def build_shard(config, rank, world, device, batch=None):
+    """Rank ``rank``'s shard: c5 splits its 8 KV heads over the ranks (strong
+    scaling); the other shapes give every rank a full-size shard with its own
+    seed (weak scaling by KV head)."""
+    from paged_attention import workloads
+    if config == "c5":
+        return workloads.c5(device, rank=rank, world=world, batch=batch)
+    return workloads.CONFIGS[config](device, seed=SEEDS[config] + 1000 * rank)
+
+
+def max_over_ranks(values, dist, device):
+    """Element-wise max of per-rank timings (all_reduce MAX; identity at N=1)."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def gather_and_verify(out, local_ok, config, rank, world, dist, device, batch=None,
+                      rows=None):
+    """All-gather every rank's output; rank 0 rebuilds each shard's inputs from
+    its seed and checks sampled rows against the oracle. Returns the verdict,
+    agreed by all ranks (all_reduce MIN)."""
+    import oracle
+    gathered = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(gathered, out)
+    ok = bool(local_ok)
+    if rank == 0:
+        for r in range(world):
+            wr = build_shard(config, r, world, device, batch=batch)
+            sel = rows if rows is not None else [0, wr.batch - 1]
+            ro, _ = oracle.decode_reference(wr.q, wr.k_cache, wr.v_cache, wr.block_table,
+                                            wr.seq_len, wr.block_size, batch_indices=sel)
+            got = gathered[r].float().cpu()[sel]
+            ref = ro[sel]
+            ok &= bool(((got - ref).abs() <= 2e-3 + 1e-2 * ref.abs()).all())
+            del wr
+    flag = torch.tensor([1 if ok else 0], device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return bool(flag.item())
 
 
 # ----------------------------------------------------------------------------- b200 arm
@@ -150,12 +211,8 @@ def run_b200(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
 
-    # Each rank builds its own shard: c2's shape with a rank-specific seed.
-    builder = workloads.CONFIGS[args.config]
-    if args.config == "c5":
-        w = builder(dev, rank=rank, world=world)
-    else:
-        w = builder(dev, seed={"c1": 1, "c2": 2, "c3": 3, "c4": 4}[args.config] + 1000 * rank)
+    # Each rank builds its own shard (own seed / own KV heads).
+    w = build_shard(args.config, rank, world, dev)
     nbytes = w.effective_bytes()
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     ws = pa.DecodeWorkspace(dev)
@@ -276,31 +333,12 @@ def run_b200(args, rank, world, local_rank):
     e2e_ok = torch.equal(o_host, out.cpu())
 
     # ---- max over ranks
-    vals = torch.tensor([eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"]],
-                        dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    eager_mean, graph_mean, e2e_mean, sync_med = vals.tolist()
+    eager_mean, graph_mean, e2e_mean, sync_med = max_over_ranks(
+        [eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"]], dist, dev)
 
     # ---- verification all-gather over NCCL (outside the timed region)
-    gathered_ok = True
     if dist is not None:
-        gathered = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(gathered, out)
-        if rank == 0:
-            for r in range(world):
-                wr = builder(dev, rank=r, world=world) if args.config == "c5" else builder(
-                    dev, seed={"c1": 1, "c2": 2, "c3": 3, "c4": 4}[args.config] + 1000 * r)
-                rows = [0, wr.batch - 1]
-                ro_r, _ = oracle.decode_reference(wr.q, wr.k_cache, wr.v_cache, wr.block_table,
-                                                  wr.seq_len, wr.block_size, batch_indices=rows)
-                got = gathered[r].float().cpu()[rows]
-                gathered_ok &= bool(((got - ro_r[rows]).abs() <=
-                                     2e-3 + 1e-2 * ro_r[rows].abs()).all())
-                del wr
-        flag = torch.tensor([1 if (parity_ok and gathered_ok) else 0], device=dev)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        parity_ok = bool(flag.item())
+        parity_ok = gather_and_verify(out, parity_ok, args.config, rank, world, dist, dev)
 
     status = ws.read_status()
 
@@ -324,7 +362,7 @@ def run_b200(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(eager_mean, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.config == "c5" else "weak",
         "vs_baseline": None,
         "dtype": str(w.dtype).replace("torch.", "").replace("float16", "f16").replace(
             "bfloat16", "bf16"),
@@ -337,7 +375,7 @@ def run_b200(args, rank, world, local_rank):
             "kv_bytes_per_rank": nbytes,
             "l2": "flushed before every step (512 MB write)",
             "schedule": "token-balanced persistent",
-            "parallelism": f"kv-head shards x{world}" if world > 1 else "single GPU",
+            "parallelism": (f"kv-head shards x{world}" if world > 1 else "single GPU"),
         },
         "us_per_step": {"eager": round(eager_mean * 1e3, 2), "graph": round(graph_mean * 1e3, 2),
                         "eager_host_sync": round(sync_med * 1e3, 2),

@@ -96,6 +96,9 @@ typedef struct pa_decode_params {
   int32_t* counters;           /* zero-filled once by the caller; the kernel leaves it zeroed */
   size_t counter_count;
   uint32_t* status;            /* optional device word, PA_STATUS_* bits OR-ed in */
+  /* 0: automatic. 1..5: a fixed kernel variant (tile tokens x warps x ring
+   * depth), for tuning; see the variant table in csrc/pa_decode.cu. */
+  int32_t kernel_variant;
 } pa_decode_params;
 
 /* Bytes of workspace and number of int32 arrival counters pa_decode needs for

@@ -1,10 +1,10 @@
 // pa_decode.cu -- paged-attention decode for B200 (sm_100a).
 //
 // One persistent kernel per decode step. Each warp is an independent worker:
-// it owns a contiguous range of 32-token tiles of the flattened
+// it owns a contiguous range of TILE-token tiles of the flattened
 // (sequence, kv-head, tile) space, streams the K/V page rows of those tiles
-// into shared memory with TMA (cp.async.bulk.tensor, 128-byte swizzle, a
-// 3-deep mbarrier ring per warp), and runs the FP32 online softmax with both
+// into shared memory with TMA (cp.async.bulk.tensor, 128-byte swizzle, an
+// NS-deep mbarrier ring per warp), and runs the FP32 online softmax with both
 // products on the tensor cores (mma.sync m16n8k16, K and V fed by ldmatrix).
 // A worker whose range covers a whole (sequence, kv-head) writes the final
 // output; otherwise it stores a partial (normalised O, LSE) and the last
@@ -36,21 +36,30 @@
 namespace pa {
 
 constexpr int kD = 128;             // head_dim
-constexpr int kTile = 32;           // tokens per pipeline stage
-constexpr int kWarps = 4;           // worker warps per CTA
-constexpr int kStages = 3;          // ring depth per worker
-constexpr int kHalfBytes = kTile * 128;          // one 64-dim half of a K or V tile
-constexpr int kKVBytes = 2 * kHalfBytes;         // one K (or V) tile: 8 KB
-constexpr int kQBytes = 8 * kD * 2;              // up to 8 query heads
-constexpr int kStageBytes = 2 * kKVBytes + kQBytes;   // 18 KB, multiple of 1 KB
-constexpr int kCumMax = 2048;       // rows whose tile prefix sum fits in shared memory
-constexpr int kSmemBytes = kWarps * kStages * kStageBytes + (kCumMax + 1) * 4 + 1024 + 128;
+constexpr int kCumMax = 1024;       // rows whose tile prefix sum fits in shared memory
+constexpr int kDescInts = 12;       // per-stage tile descriptor
 constexpr float kSentinel = -1e30f;     // split_kv_kernel.py:8
 constexpr float kValidLse = -1e29f;     // split_kv_kernel.py:9
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per barrier wait
 constexpr unsigned kFull = 0xffffffffu;
+
+// Shared-memory plan of one kernel variant.
+template <bool kDup, int TILE, int NW, int NS>
+struct Cfg {
+  static constexpr int kMB = TILE / 16;            // 16-token m-blocks per tile
+  // A K (or V) tile is stored box-major: for each TMA box of R token rows,
+  // [half 0: R rows x 128 B][half 1: R rows x 128 B], each half 128-byte swizzled.
+  static constexpr int kKV = TILE * 256;           // one K (or V) tile
+  static constexpr int kQ = kDup ? 1024 : 2048;    // query rows loaded with a piece's first tile
+  static constexpr int kStage = 2 * kKV + kQ;      // multiple of 1 KB (swizzle atom)
+  static constexpr int kStagesBytes = NW * NS * kStage;
+  static constexpr int kBarOff = kStagesBytes;
+  static constexpr int kDescOff = kBarOff + NW * NS * 8;
+  static constexpr int kCumOff = kDescOff + NW * NS * kDescInts * 4;
+  static constexpr int kSmem = kCumOff + (kCumMax + 1) * 4 + 1024;  // + alignment slack
+};
 
 struct KParams {
   const char* q;            // bytes
@@ -62,21 +71,28 @@ struct KParams {
   long long bt_sb;          // elements
   int max_blocks;
   const int* seq_lens;
-  int seq_len;              // clamped uniform length (seq_lens == nullptr)
+  int seq_len;              // uniform length (seq_lens == nullptr)
   int B, Hq, Hkv, G, QC, bs, NB;
-  int nseg;                 // Hkv * QC segments per row
+  int bs_log2;              // log2(bs) if a power of two, else -1
   int ns;                   // 0: balanced schedule
-  float scale_log2;
+  float scale_log2;         // softmax scale * log2(e)
   float* o_part;            // split: [B, Hq, ns, D]; balanced: [2W, 8, D]
   float* lse_part;          // split: [B, Hq, ns];    balanced: [2W, 8]
   int* counters;
   unsigned* status;
-  int R;                    // rows per TMA box (gcd(bs, kTile))
-  int spt;                  // boxes per tile (kTile / R)
+  int R;                    // rows per TMA box (gcd(bs, TILE))
+  int lspt;                 // log2(TILE / R): boxes per tile
+  int lR;                   // log2(R)
+  int map5d;                // 1: one 5-D copy per box covers both 64-dim halves
   int W;                    // workers
   int use_cum;              // balanced + seq_lens: prefix sums in shared memory
+  int slot_cols;            // balanced partial slot width: min(G, 8) query heads
+  int static_pct;           // balanced: share of units in static per-worker ranges (%)
+  int dyn_per_worker;       // balanced: dynamic ranges per worker (upper bound)
+  int n_seg_counters;       // arrival counters before the two schedule counters
+  int hybrid_min_units;     // balanced: dynamic ranges only above this many units per worker
+  int min_dyn_units;        // balanced: smallest dynamic range
 };
-
 // ----------------------------------------------------------------------------
 // PTX helpers
 // ----------------------------------------------------------------------------
@@ -132,6 +148,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, int c4, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
                                           uint32_t bar) {
   asm volatile(
@@ -182,6 +207,14 @@ struct Mma<__half> {
   __device__ __forceinline__ static uint16_t from_float(float x) {
     return __half_as_ushort(__float2half_rn(x));
   }
+  // Packed (p0, p1) rounded to the operand type (hi) and the rounded residual (lo).
+  __device__ __forceinline__ static void split2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(p0, p1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
 };
 
 template <>
@@ -203,6 +236,13 @@ struct Mma<__nv_bfloat16> {
   __device__ __forceinline__ static uint16_t from_float(float x) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(x));
   }
+  __device__ __forceinline__ static void split2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(p0, p1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+  }
 };
 
 __device__ __forceinline__ uint32_t pack16(uint16_t lo, uint16_t hi) {
@@ -210,21 +250,25 @@ __device__ __forceinline__ uint32_t pack16(uint16_t lo, uint16_t hi) {
 }
 
 // ----------------------------------------------------------------------------
+
+// ----------------------------------------------------------------------------
 // Work decomposition
 // ----------------------------------------------------------------------------
-struct Tile {
-  int b, seg, tile;   // row, segment within the row (kvh * QC + qc), tile within the segment
-  int t0, t1;         // token range of this worker's piece of the segment
-  int seg_lo, seg_hi; // unit range of the segment (balanced) / split index in seg_lo (split)
-  bool first, last, whole;
-};
-
-struct Work {
-  int n;                // tiles of this worker
-  int u0, u1;           // balanced: unit range
-  int per;              // balanced: units per worker
-  int b, seg, s, t0, t1;  // split: the one piece
-};
+// A unit is one TILE-token tile of one segment; a segment is one row b and one
+// (kv head, query chunk) pair, query chunk qc holding query heads
+// kvh*G + qc*8 .. +min(8, G - qc*8).
+//
+// Balanced schedule: units are flattened in (b, kvh, qc, tile) order and cut
+// into ranges. Range r < W (one per worker) is static, [r*Ps, min(Us, (r+1)*Ps));
+// ranges r >= W cover the remaining units in small dynamic chunks of CUd units,
+// taken in order from a global counter by whichever worker is free. A worker
+// first drains its static range, then takes dynamic ranges until none is left,
+// which absorbs per-SM bandwidth differences at the tail. A piece is the part
+// of one segment inside one range; its partial lives in slot 2r (piece starts
+// the range) or 2r+1 (piece ends the range).
+//
+// Split schedule (the reference's): worker w owns split s of one segment; its
+// single range is the split's tiles, and its partial is the split's row.
 
 __device__ __forceinline__ int clamp_len(const KParams& p, int s, bool& bad) {
   const int cap = p.max_blocks * p.bs;
@@ -249,78 +293,263 @@ __device__ __forceinline__ int find_row(const int* cum, int B, int u) {
   return lo;
 }
 
-__device__ __forceinline__ void get_tile(const KParams& p, const int* cum, const Work& w, int i,
-                                         Tile& t) {
-  if (p.ns == 0) {
-    const int u = w.u0 + i;
-    int b, base, S, nt;
-    if (p.use_cum) {
-      b = find_row(cum, p.B, u);
-      base = cum[b];
-      S = row_len(p, b);
-      nt = (S + kTile - 1) / kTile;
-    } else {
-      S = p.seq_len;
-      nt = (S + kTile - 1) / kTile;
-      const int per_row = p.nseg * nt;
-      b = u / per_row;
-      base = b * per_row;
-    }
-    const int r = u - base;
-    t.b = b;
-    t.seg = r / nt;
-    t.tile = r - t.seg * nt;
-    t.seg_lo = base + t.seg * nt;
-    t.seg_hi = t.seg_lo + nt;
-    const int plo = max(t.seg_lo, w.u0), phi = min(t.seg_hi, w.u1);
-    t.first = (u == plo);
-    t.last = (u == phi - 1);
-    t.whole = (plo == t.seg_lo) && (phi == t.seg_hi);
-    t.t0 = (plo - t.seg_lo) * kTile;
-    t.t1 = min(S, (phi - t.seg_lo) * kTile);
+struct Sched {        // balanced schedule, identical in every CTA
+  int U, Ps, Us, CUd, nd;
+};
+
+struct Work {         // split schedule: the worker's one piece
+  int b, kvh, qc, s, t0, t1, tl0, n;
+};
+
+// Position of a tile: segment, tile within it, segment length in tiles.
+struct Cursor {
+  int b, kvh, qc;
+  int tile, nt, S;
+  int seg_lo;         // unit index of the segment's tile 0 (balanced)
+};
+
+template <int TILE>
+__device__ __forceinline__ void decode_unit(Cursor& c, const KParams& p, const int* cum, int u) {
+  int row_base;
+  if (p.use_cum) {
+    c.b = find_row(cum, p.B, u);
+    row_base = cum[c.b];
+    c.S = row_len(p, c.b);
   } else {
-    t.b = w.b;
-    t.seg = w.seg;
-    t.tile = w.t0 / kTile + i;
-    t.t0 = w.t0;
-    t.t1 = w.t1;
-    t.seg_lo = w.s;
-    t.seg_hi = 0;
-    t.first = (i == 0);
-    t.last = (i == w.n - 1);
-    t.whole = false;
+    c.S = p.seq_len;
+    const int per_row = p.Hkv * p.QC * ((c.S + TILE - 1) / TILE);
+    c.b = u / per_row;
+    row_base = c.b * per_row;
+  }
+  c.nt = (c.S + TILE - 1) / TILE;
+  const int r = u - row_base;
+  const int seg = r / c.nt;
+  c.tile = r - seg * c.nt;
+  c.kvh = seg / p.QC;
+  c.qc = seg - c.kvh * p.QC;
+  c.seg_lo = row_base + seg * c.nt;
+}
+
+// Next unit in flattened order (balanced).
+template <int TILE>
+__device__ __forceinline__ void cursor_next(Cursor& c, const KParams& p) {
+  if (++c.tile < c.nt) return;
+  c.tile = 0;
+  c.seg_lo += c.nt;
+  if (++c.qc < p.QC) return;
+  c.qc = 0;
+  if (++c.kvh < p.Hkv) return;
+  c.kvh = 0;
+  do {   // next row that owns tiles (rows of length 0 own none)
+    if (c.b + 1 >= p.B) { c.nt = 1; return; }   // past the end: never used
+    ++c.b;
+    c.S = row_len(p, c.b);
+    c.nt = (c.S + TILE - 1) / TILE;
+  } while (c.nt == 0);
+}
+
+__device__ __forceinline__ void range_bounds(const KParams& p, const Sched& sc, int r, int& r0,
+                                             int& r1) {
+  if (r < p.W) {
+    r0 = min(sc.U, r * sc.Ps);
+    r1 = min(sc.Us, r0 + sc.Ps);
+  } else {
+    r0 = sc.Us + (r - p.W) * sc.CUd;
+    r1 = min(sc.U, r0 + sc.CUd);
   }
 }
 
-// Physical block of this lane's TMA box in window `win`, or INT_MIN when the box
-// holds no token of the piece (never loaded, masked by the consumer).
-__device__ __forceinline__ int fetch_window(const KParams& p, const int* cum, const Work& w, int win,
-                                            int lane, int wt) {
-  const int i = win * wt + lane / p.spt;
-  if (i >= w.n) return INT_MIN;
-  Tile t;
-  get_tile(p, cum, w, i, t);
-  const int tt = t.tile * kTile + (lane % p.spt) * p.R;
-  if (tt >= t.t1 || tt + p.R <= t.t0) return INT_MIN;
-  return __ldg(p.bt + static_cast<long long>(t.b) * p.bt_sb + tt / p.bs);
+// Piece of the cursor's tile inside range [r0, r1) (balanced): token range,
+// flags (1 first tile of the piece, 2 last, 4 piece == whole segment), slot.
+template <int TILE>
+__device__ __forceinline__ void piece_of(const Cursor& c, int r, int r0, int r1, int& t0, int& t1,
+                                         int& flags, int& slot) {
+  const int u = c.seg_lo + c.tile;
+  const int seg_hi = c.seg_lo + c.nt;
+  const int plo = max(c.seg_lo, r0), phi = min(seg_hi, r1);
+  t0 = (plo - c.seg_lo) * TILE;
+  t1 = min(c.S, (phi - c.seg_lo) * TILE);
+  flags = (u == plo ? 1 : 0) | (u == phi - 1 ? 2 : 0) | ((plo == c.seg_lo && phi == seg_hi) ? 4 : 0);
+  slot = 2 * r + (plo == r0 ? 0 : 1);
 }
 
 __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
   if (p.status) atomicOr(p.status, bits);
 }
 
+// Block-table page and slot of this lane's TMA box in a batch of tiles: lane L
+// serves box (L & (spt-1)) of tile (L >> lspt) of the batch [u0, u1) of range
+// r. INT_MIN: the box holds no token of its piece (not loaded; the consumer
+// masks it). One load instruction per batch and lane.
+template <int TILE>
+__device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, const Sched& sc,
+                                            const Work& w, int r, int r0, int r1, int u0, int u1,
+                                            int lane, int& phys, int& slot) {
+  const int ord = lane >> p.lspt;
+  const int j = lane & ((1 << p.lspt) - 1);
+  long long off = -1;
+  slot = 0;
+  if (u0 + ord < u1) {
+    int tile, b, t0, t1;
+    if (p.ns == 0) {
+      Cursor c;
+      decode_unit<TILE>(c, p, cum, u0 + ord);
+      int fl, sl;
+      piece_of<TILE>(c, r, r0, r1, t0, t1, fl, sl);
+      tile = c.tile;
+      b = c.b;
+    } else {
+      tile = w.tl0 + u0 + ord;
+      b = w.b;
+      t0 = w.t0;
+      t1 = w.t1;
+    }
+    const int tt = tile * TILE + j * p.R;
+    if (tt < t1 && tt + p.R > t0) {
+      const int lp = p.bs_log2 >= 0 ? (tt >> p.bs_log2) : tt / p.bs;
+      off = static_cast<long long>(b) * p.bt_sb + lp;
+      slot = tt - lp * p.bs;
+    }
+  }
+  phys = off >= 0 ? __ldg(p.bt + off) : INT_MIN;
+}
+
+// ----------------------------------------------------------------------------
+// Merge of one segment's partials (the last arriving piece runs it)
+// ----------------------------------------------------------------------------
+// split_kv_kernel.py:101-122: skip lse <= -1e29, merge by running max, divide
+// by max(sum, 1e-20); a segment with no valid piece outputs 0 and LSE -1e30.
+// Each lane owns 4 of the 128 dims.
+struct PieceSet {     // the pieces of one segment
+  int n;              // number of pieces
+  int n_static, r_first, d_first, seg_lo;
+};
+
+__device__ __forceinline__ PieceSet pieces_of(const KParams& p, const Sched& sc, int seg_lo,
+                                              int seg_hi) {
+  PieceSet ps;
+  ps.seg_lo = seg_lo;
+  ps.n_static = 0;
+  ps.r_first = 0;
+  ps.d_first = 0;
+  if (sc.Ps > 0 && seg_lo < sc.Us) {
+    ps.r_first = seg_lo / sc.Ps;
+    ps.n_static = (min(seg_hi, sc.Us) - 1) / sc.Ps - ps.r_first + 1;
+  }
+  int n_dyn = 0;
+  if (seg_hi > sc.Us) {
+    ps.d_first = (max(seg_lo, sc.Us) - sc.Us) / sc.CUd;
+    n_dyn = (seg_hi - 1 - sc.Us) / sc.CUd - ps.d_first + 1;
+  }
+  ps.n = ps.n_static + n_dyn;
+  return ps;
+}
+
+template <typename T>
+__device__ __forceinline__ void merge_segment(const KParams& p, const Sched& sc, int b, int kvh,
+                                              int qc, int gc, const PieceSet& ps, int lane) {
+  constexpr int kBatch = 8;   // partial rows in flight per lane
+  const int n = (p.ns == 0) ? ps.n : p.ns;
+  for (int j = 0; j < gc; ++j) {
+    const int hq = kvh * p.G + qc * 8 + j;
+    auto part = [&](int k, const float*& op, const float*& lp) {
+      if (p.ns == 0) {
+        int r, r_start;
+        if (k < ps.n_static) {
+          r = ps.r_first + k;
+          r_start = r * sc.Ps;
+        } else {
+          const int d = ps.d_first + (k - ps.n_static);
+          r = p.W + d;
+          r_start = sc.Us + d * sc.CUd;
+        }
+        const long long sl = 2ll * r + (max(ps.seg_lo, r_start) == r_start ? 0 : 1);
+        op = p.o_part + (sl * p.slot_cols + j) * kD;
+        lp = p.lse_part + sl * p.slot_cols + j;
+      } else {
+        const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + k;
+        op = p.o_part + row * kD;
+        lp = p.lse_part + row;
+      }
+    };
+    auto row4 = [&](int k) {
+      const float* op;
+      const float* lp;
+      part(k, op, lp);
+      return __ldcg(reinterpret_cast<const float4*>(op) + lane);
+    };
+    auto lse_of = [&](int k) {
+      const float* op;
+      const float* lp;
+      part(k, op, lp);
+      return __ldcg(lp);
+    };
+    // One round trip for the common case: the LSEs of the first 32 pieces
+    // (one per lane) and the rows of the first kBatch pieces are in flight together.
+    const float l0 = (lane < n) ? lse_of(lane) : kValidLse;
+    float4 v[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? row4(u) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float gmax = (l0 > kValidLse) ? l0 : kValidLse;
+    for (int k = lane + 32; k < n; k += 32) {
+      const float l = lse_of(k);
+      if (l > kValidLse) gmax = fmaxf(gmax, l);
+    }
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float gsum = 0.f;
+    for (int base = 0; base < n; base += 32) {
+      const float lb = (base == 0) ? l0 : ((base + lane < n) ? lse_of(base + lane) : kValidLse);
+      const float wl = (lb > kValidLse) ? exp2f((lb - gmax) * kLog2e) : 0.f;
+      float ws = wl;
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) ws += __shfl_xor_sync(kFull, ws, o2);
+      gsum += ws;
+      const int cnt = min(32, n - base);
+      for (int k0 = 0; k0 < cnt; k0 += kBatch) {
+        if (base + k0 > 0) {
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u)
+            v[u] = (k0 + u < cnt) ? row4(base + k0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const float wgt = __shfl_sync(kFull, wl, (k0 + u) & 31);
+          if (k0 + u < cnt && wgt > 0.f) {
+            a4.x = fmaf(wgt, v[u].x, a4.x);
+            a4.y = fmaf(wgt, v[u].y, a4.y);
+            a4.z = fmaf(wgt, v[u].z, a4.z);
+            a4.w = fmaf(wgt, v[u].w, a4.w);
+          }
+        }
+      }
+    }
+    const float inv = 1.f / fmaxf(gsum, 1e-20f);
+    char* dst = p.out + b * p.o_sb + hq * p.o_sh + lane * 8;
+    const uint32_t lo = pack16(Mma<T>::from_float(a4.x * inv), Mma<T>::from_float(a4.y * inv));
+    const uint32_t hi = pack16(Mma<T>::from_float(a4.z * inv), Mma<T>::from_float(a4.w * inv));
+    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+    if (lane == 0 && p.lse) p.lse[b * p.Hq + hq] = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
+  }
+}
+
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
-template <typename T, bool kDup>
-__global__ void __launch_bounds__(kWarps * 32, 1)
+template <typename T, bool kDup, int TILE, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1)
     pa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const KParams p) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  using C = Cfg<kDup, TILE, NW, NS>;
+  constexpr int kMB = C::kMB;
+  extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * kStages * kStageBytes);
-  int* cum = reinterpret_cast<int*>(bars + kWarps * kStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  int* descs = reinterpret_cast<int*>(smem + C::kDescOff);
+  int* cum = reinterpret_cast<int*>(smem + C::kCumOff);
+  __shared__ int warp_tot[NW];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -330,13 +559,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
   }
   if (lane == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(smem_u32(&bars[warp * kStages + s]), 1);
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&bars[warp * NS + s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
 
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
   if (p.ns == 0 && p.use_cum) {
     const int B = p.B;
+    const int nseg = p.Hkv * p.QC;
     const int chunk = (B + blockDim.x - 1) / blockDim.x;
     const int lo = min(B, static_cast<int>(threadIdx.x) * chunk);
     const int hi = min(B, lo + chunk);
@@ -344,17 +574,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     int local = 0;
     for (int b = lo; b < hi; ++b) {
       const int S = clamp_len(p, __ldg(p.seq_lens + b), bad);
-      local += p.nseg * ((S + kTile - 1) / kTile);
+      local += nseg * ((S + TILE - 1) / TILE);
     }
     if (bad && blockIdx.x == 0) flag(p, PA_STATUS_BAD_SEQLEN);
-    // exclusive scan of `local` over the block
     int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int v = __shfl_up_sync(kFull, incl, o);
       if (lane >= o) incl += v;
     }
-    __shared__ int warp_tot[kWarps];
     if (lane == 31) warp_tot[warp] = incl;
     __syncthreads();
     int before = 0;
@@ -363,7 +591,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     for (int b = lo; b < hi; ++b) {
       cum[b] = run;
       const int S = clamp_len(p, __ldg(p.seq_lens + b), bad);
-      run += p.nseg * ((S + kTile - 1) / kTile);
+      run += nseg * ((S + TILE - 1) / TILE);
     }
     if (threadIdx.x == blockDim.x - 1) cum[B] = before + incl;
   }
@@ -383,49 +611,108 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
   }
 
-  // ---------------------------------------------------------------- my work
+  // ---------------------------------------------------------------- schedule
   const int wid = warp * gridDim.x + blockIdx.x;
+  const int G = p.G;
+  const int spt_mask = (1 << p.lspt) - 1;
+  const int bt_tiles = 32 >> p.lspt;          // tiles per page batch (one box per lane)
+  int* sched_ctr = p.counters + p.n_seg_counters;   // [0] next dynamic range, [1] workers done
+  Sched sc;
+  sc.U = sc.Ps = sc.Us = sc.nd = 0;
+  sc.CUd = 1;
   Work w;
+  w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
+  int rc = -1, r0c = 0, r1c = 0, u0c = 0, u1c = 0;   // current page batch: range, units
+  int pend = 0;                                       // lane 0: prefetched dynamic range id
   if (p.ns == 0) {
-    const int U = p.use_cum ? cum[p.B] : p.B * p.nseg * ((p.seq_len + kTile - 1) / kTile);
-    w.per = max(1, (U + p.W - 1) / p.W);
-    w.u0 = min(U, wid * w.per);
-    w.u1 = min(U, w.u0 + w.per);
-    w.n = w.u1 - w.u0;
+    const int W = p.W;
+    sc.U = p.use_cum ? cum[p.B] : p.B * p.Hkv * p.QC * ((p.seq_len + TILE - 1) / TILE);
+    if (sc.U <= p.hybrid_min_units * W) {
+      // small step: static ranges only (dynamic ranges would cost more than the tail)
+      sc.Ps = max(1, (sc.U + W - 1) / W);
+      sc.Us = sc.U;
+    } else {
+      sc.Ps = static_cast<int>(static_cast<long long>(sc.U) * p.static_pct / (100ll * W));
+      sc.Us = sc.Ps * W;
+      const int ud = sc.U - sc.Us;
+      const int want = p.dyn_per_worker * W;
+      sc.CUd = max(p.min_dyn_units, (ud + want - 1) / want);
+      sc.nd = (ud + sc.CUd - 1) / sc.CUd;
+    }
+    rc = wid;
+    range_bounds(p, sc, rc, r0c, r1c);
+    if (r0c >= r1c) {
+      rc = -1;
+      if (sc.nd > 0) {
+        if (lane == 0) pend = W + atomicAdd(sched_ctr, 1);
+        const int nr = __shfl_sync(kFull, pend, 0);
+        if (nr < W + sc.nd) {
+          rc = nr;
+          range_bounds(p, sc, rc, r0c, r1c);
+        }
+      }
+    }
+    u0c = r0c;
+    u1c = min(r1c, r0c + bt_tiles);
+    // The id of the next dynamic range is requested one page batch before it is
+    // needed: when the batch being prepared is the last of its range.
+    if (rc >= 0 && sc.nd > 0 && u1c >= r1c && lane == 0) pend = W + atomicAdd(sched_ctr, 1);
   } else {
-    const int total = p.B * p.nseg * p.ns;
+    const int total = p.B * p.Hkv * p.QC * p.ns;
     if (wid >= total) return;
     w.s = wid % p.ns;
     const int rs = wid / p.ns;
-    w.seg = rs % p.nseg;
-    w.b = rs / p.nseg;
+    const int seg = rs % (p.Hkv * p.QC);
+    w.b = rs / (p.Hkv * p.QC);
+    w.kvh = seg / p.QC;
+    w.qc = seg - w.kvh * p.QC;
     bool bad = false;
     const int S = p.seq_lens ? clamp_len(p, __ldg(p.seq_lens + w.b), bad) : p.seq_len;
-    if (bad && w.s == 0 && w.seg == 0) flag(p, PA_STATUS_BAD_SEQLEN);
+    if (bad && w.s == 0 && seg == 0) flag(p, PA_STATUS_BAD_SEQLEN);
     const int ss = (S + p.ns - 1) / p.ns;       // torch_kernel.py:30
     w.t0 = w.s * ss;
     w.t1 = min(w.t0 + ss, S);
-    w.n = (w.t0 < w.t1) ? ((w.t1 - 1) / kTile - w.t0 / kTile + 1) : 0;
+    w.tl0 = w.t0 / TILE;
+    w.n = (w.t0 < w.t1) ? ((w.t1 - 1) / TILE - w.tl0 + 1) : 0;
+    if (w.n > 0) {
+      rc = w.s;
+      r0c = 0;
+      r1c = w.n;
+      u0c = 0;
+      u1c = min(w.n, bt_tiles);
+    }
   }
 
-  const uint32_t stage0 = smem_u32(smem + warp * kStages * kStageBytes);
-  const uint32_t bar0 = smem_u32(&bars[warp * kStages]);
-  const int wt = 32 / p.spt;  // tiles per page-index window
-
-  // Output-side helpers.
-  const int G = p.G;
-  auto seg_heads = [&](int seg, int& kvh, int& qc, int& gc) {
-    kvh = seg / p.QC;
-    qc = seg - kvh * p.QC;
-    gc = min(8, G - qc * 8);
+  // Successor of a page batch: the rest of its range, else the next dynamic range.
+  auto succ = [&](int& r, int& r0, int& r1, int& u0, int& u1) {
+    if (r < 0) return;
+    if (u1 < r1) {
+      u0 = u1;
+      u1 = min(r1, u0 + bt_tiles);
+    } else {
+      r = -1;
+      if (p.ns != 0 || sc.nd == 0) return;
+      const int nr = __shfl_sync(kFull, pend, 0);
+      if (nr >= p.W + sc.nd) return;
+      r = nr;
+      range_bounds(p, sc, r, r0, r1);
+      u0 = r0;
+      u1 = min(r1, r0 + bt_tiles);
+    }
+    if (p.ns == 0 && sc.nd > 0 && u1 >= r1 && lane == 0) pend = p.W + atomicAdd(sched_ctr, 1);
   };
 
+  const uint32_t stage0 = smem_u32(smem + warp * NS * C::kStage);
+  const uint32_t bar0 = smem_u32(&bars[warp * NS]);
+  int* desc0 = descs + warp * NS * kDescInts;
+
+  // Split schedule, empty split (split_kv_kernel.py:32-33): the partial LSE keeps
+  // the sentinel; the last arriving split of the segment merges.
+  bool merge_empty = false;
   if (p.ns != 0 && w.n == 0) {
-    // Empty split (split_kv_kernel.py:32-33): partial LSE keeps the sentinel.
-    int kvh, qc, gc;
-    seg_heads(w.seg, kvh, qc, gc);
+    const int gc = min(8, G - w.qc * 8);
     for (int j = 0; j < gc; ++j) {
-      const int hq = kvh * G + qc * 8 + j;
+      const int hq = w.kvh * G + w.qc * 8 + j;
       const long long row = (static_cast<long long>(w.b) * p.Hq + hq) * p.ns + w.s;
       for (int d = lane; d < kD; d += 32) p.o_part[row * kD + d] = 0.f;
       if (lane == 0) p.lse_part[row] = kSentinel;
@@ -433,100 +720,168 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     __threadfence();
     __syncwarp();
     int last = 0;
-    const int cid = (w.b * p.Hkv + kvh) * p.QC + qc;
+    const int cid = (w.b * p.Hkv + w.kvh) * p.QC + w.qc;
     if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == p.ns - 1);
     last = __shfl_sync(kFull, last, 0);
     if (!last) return;
     __threadfence();
-    // fall through to the merge below with an empty tile list
+    merge_empty = true;
   }
 
-  // Page-index windows (register double buffer, one entry per lane).
-  int win = 0;
-  int pg_cur = w.n > 0 ? fetch_window(p, cum, w, 0, lane, wt) : INT_MIN;
-  int pg_nxt = w.n > wt ? fetch_window(p, cum, w, 1, lane, wt) : INT_MIN;
+  // ---- issuer: current batch (pages pg_c/sl_c), next batch (pg_n/sl_n), cursor
+  int pg_c = INT_MIN, sl_c = 0, pg_n = INT_MIN, sl_n = 0;
+  int rn = rc, r0n = r0c, r1n = r1c, u0n = u0c, u1n = u1c;
+  if (rc >= 0) batch_pages<TILE>(p, cum, sc, w, rc, r0c, r1c, u0c, u1c, lane, pg_c, sl_c);
+  succ(rn, r0n, r1n, u0n, u1n);
+  if (rn >= 0) batch_pages<TILE>(p, cum, sc, w, rn, r0n, r1n, u0n, u1n, lane, pg_n, sl_n);
+  Cursor ic;
+  ic.b = w.b;
+  ic.kvh = w.kvh;
+  ic.qc = w.qc;
+  ic.tile = w.tl0;
+  ic.nt = ic.S = ic.seg_lo = 0;
+  if (rc >= 0 && p.ns == 0) decode_unit<TILE>(ic, p, cum, u0c);
+  int ord = 0;          // tile ordinal within the current batch
+  int issued = 0;
 
-  auto issue = [&](int i, int st) {
-    if (i / wt != win) {
-      ++win;
-      pg_cur = pg_nxt;
-      pg_nxt = fetch_window(p, cum, w, win + 1, lane, wt);
+  auto issue = [&](int st) {
+    int t0, t1, fl, slot;
+    if (p.ns == 0) {
+      piece_of<TILE>(ic, rc, r0c, r1c, t0, t1, fl, slot);
+    } else {
+      const int k = u0c + ord;
+      t0 = w.t0;
+      t1 = w.t1;
+      fl = (k == 0 ? 1 : 0) | (k == w.n - 1 ? 2 : 0);
+      slot = w.s;
     }
-    Tile t;
-    get_tile(p, cum, w, i, t);
-    int kvh, qc, gc;
-    seg_heads(t.seg, kvh, qc, gc);
-    const bool mine = (lane / p.spt) == (i % wt);
-    bool valid = mine && pg_cur != INT_MIN;
-    if (valid && (pg_cur < 0 || pg_cur >= p.NB)) {
+    const int gc = min(8, G - ic.qc * 8);
+    const int src = (ord << p.lspt) + (lane & spt_mask);
+    const int phys = __shfl_sync(kFull, pg_c, src);
+    const int pslot = __shfl_sync(kFull, sl_c, src);
+    bool valid = lane <= spt_mask && phys != INT_MIN;
+    if (valid && (phys < 0 || phys >= p.NB)) {
       flag(p, PA_STATUS_BAD_BLOCK);
       valid = false;
     }
     const unsigned vm = __ballot_sync(kFull, valid);
     const uint32_t bar = bar0 + st * 8;
-    const uint32_t qbytes = t.first ? gc * kD * 2 : 0;
-    if (lane == 0) mbar_expect_tx(bar, __popc(vm) * 4 * p.R * 128 + qbytes);
+    const uint32_t sk = stage0 + st * C::kStage;
+    const bool first = fl & 1;
+    if (lane == 0) {
+      int* d = desc0 + st * kDescInts;
+      reinterpret_cast<int4*>(d)[0] = make_int4(ic.b, ic.kvh, ic.qc, ic.tile * TILE);
+      reinterpret_cast<int4*>(d)[1] = make_int4(t0, t1, ic.seg_lo, ic.seg_lo + ic.nt);
+      reinterpret_cast<int4*>(d)[2] = make_int4(fl, gc, slot, 0);
+      mbar_expect_tx(bar, __popc(vm) * 4 * p.R * 128 + (first ? gc * kD * 2 : 0));
+    }
     __syncwarp();
-    const uint32_t sk = stage0 + st * kStageBytes;
     if (valid) {
-      const int j = lane % p.spt;
-      const int tt = t.tile * kTile + j * p.R;
-      const int slot = tt % p.bs;
-      const uint32_t row_off = j * p.R * 128;
-      tma_load_4d(sk + row_off, &tmK, 0, kvh, slot, pg_cur, bar);
-      tma_load_4d(sk + kHalfBytes + row_off, &tmK, 64, kvh, slot, pg_cur, bar);
-      tma_load_4d(sk + kKVBytes + row_off, &tmV, 0, kvh, slot, pg_cur, bar);
-      tma_load_4d(sk + kKVBytes + kHalfBytes + row_off, &tmV, 64, kvh, slot, pg_cur, bar);
+      const uint32_t hs = p.R * 128;              // one half of one box
+      const uint32_t dk = sk + lane * 2 * hs;     // this lane's box
+      if (p.map5d) {
+        tma_load_5d(dk, &tmK, 0, pslot, 0, ic.kvh, phys, bar);
+        tma_load_5d(dk + C::kKV, &tmV, 0, pslot, 0, ic.kvh, phys, bar);
+      } else {
+        tma_load_4d(dk, &tmK, 0, ic.kvh, pslot, phys, bar);
+        tma_load_4d(dk + hs, &tmK, 64, ic.kvh, pslot, phys, bar);
+        tma_load_4d(dk + C::kKV, &tmV, 0, ic.kvh, pslot, phys, bar);
+        tma_load_4d(dk + C::kKV + hs, &tmV, 64, ic.kvh, pslot, phys, bar);
+      }
     }
-    if (t.first && lane < gc) {
-      const int hq = kvh * G + qc * 8 + lane;
-      bulk_load(sk + 2 * kKVBytes + lane * kD * 2, p.q + t.b * p.q_sb + hq * p.q_sh, kD * 2, bar);
+    if (first && lane < gc) {
+      const int hq = ic.kvh * G + ic.qc * 8 + lane;
+      bulk_load(sk + 2 * C::kKV + lane * kD * 2, p.q + ic.b * p.q_sb + hq * p.q_sh, kD * 2, bar);
     }
+    ++issued;
+    // advance to the next tile
+    if (u0c + ++ord < u1c) {
+      if (p.ns == 0) cursor_next<TILE>(ic, p); else ++ic.tile;
+      return;
+    }
+    const bool same_range = (rn == rc);
+    rc = rn;
+    r0c = r0n;
+    r1c = r1n;
+    u0c = u0n;
+    u1c = u1n;
+    pg_c = pg_n;
+    sl_c = sl_n;
+    ord = 0;
+    if (rc < 0) return;
+    succ(rn, r0n, r1n, u0n, u1n);
+    if (rn >= 0) batch_pages<TILE>(p, cum, sc, w, rn, r0n, r1n, u0n, u1n, lane, pg_n, sl_n);
+    if (p.ns != 0) ++ic.tile;
+    else if (same_range) cursor_next<TILE>(ic, p);
+    else decode_unit<TILE>(ic, p, cum, u0c);
   };
 
-  const int npro = min(kStages, w.n);
-  for (int i = 0; i < npro; ++i) issue(i, i);
+  for (int s = 0; s < NS && rc >= 0; ++s) issue(s);
 
-  // Consumer state.
+  // ---- consumer state
   uint32_t qf[8][2];
   float acc[8][4];
   float m_run[2], l_run[2];
   uint32_t phase = 0;
+  uint32_t mask_hi = 0, mask_lo = 0;   // which 16-bit halves carry hi / lo of p
+  const int qd = lane & 3;             // column pair: columns 2*qd, 2*qd+1
+  const int rr = lane >> 2;            // fragment row
+  const float scl = p.scale_log2;
+
+  // ldmatrix lane offsets in the box-major, 128-byte-swizzled tile: token row r
+  // sits at r*128 + (r/R)*R*128 (box start plus the other half of earlier
+  // boxes), 16-byte chunk c of a half at ((c ^ (r & 7)) << 4), half 1 at +R*128.
+  const uint32_t hs = p.R * 128;
+  uint32_t offk[kMB], offv[kMB], swzk[4], swzv[4];
+  {
+    const int x = lane & 7;
+    const int rk = ((lane >> 3) & 1) * 8 + x, yk = (lane >> 4) ^ x;
+    const int rv = (lane >> 4) * 8 + x, yv = ((lane >> 3) & 1) ^ x;
+#pragma unroll
+    for (int mb = 0; mb < kMB; ++mb) {
+      const int r1 = mb * 16 + rk, r2 = mb * 16 + rv;
+      offk[mb] = r1 * 128 + ((r1 >> p.lR) << p.lR) * 128;
+      offv[mb] = r2 * 128 + ((r2 >> p.lR) << p.lR) * 128;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      swzk[j] = ((2 * j) ^ yk) << 4;
+      swzv[j] = ((2 * j) ^ yv) << 4;
+    }
+  }
+
   bool aborted = false;
-
-  const int qd = lane & 3;     // column pair index: columns 2*qd, 2*qd+1
-  const int rr = lane >> 2;    // fragment row
-
-  for (int i = 0; i < w.n; ++i) {
-    const int st = i % kStages;
-    Tile t;
-    get_tile(p, cum, w, i, t);
-    int kvh, qc, gc;
-    seg_heads(t.seg, kvh, qc, gc);
-    const uint32_t sk = stage0 + st * kStageBytes;
-    const uint32_t sv = sk + kKVBytes;
-    const uint32_t sq = sk + 2 * kKVBytes;
+  int st = 0;
+  for (int i = 0; i < issued; ++i) {
+    const uint32_t sk = stage0 + st * C::kStage;
+    const uint32_t sv = sk + C::kKV;
+    const uint32_t sq = sk + 2 * C::kKV;
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
       flag(p, PA_STATUS_TIMEOUT);
+      // drain the copies still in flight for the other stages (bounded), then leave
+      for (int k = 1; k < NS && i + k < issued; ++k) {
+        const int s2 = (st + k) % NS;
+        mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1);
+      }
       aborted = true;
-      // drain the copies still in flight for the other stages (bounded)
-      for (int k = i + 1; k < min(w.n, i + kStages); ++k)
-        mbar_wait(bar0 + (k % kStages) * 8, (phase >> (k % kStages)) & 1);
       break;
     }
     phase ^= 1u << st;
+    const int* d = desc0 + st * kDescInts;
+    const int4 d0 = reinterpret_cast<const int4*>(d)[0];
+    const int4 d1 = reinterpret_cast<const int4*>(d)[1];
+    const int4 d2 = reinterpret_cast<const int4*>(d)[2];
+    const int tb = d0.w, t0 = d1.x, t1 = d1.y, fl = d2.x, gc = d2.y;
 
-    if (t.first) {
+    if (fl & 1) {
       // Query fragments (B operand of S^T = K Q^T): column n -> query head.
+      const int n = rr;
+      const int head = kDup ? (n < 2 * gc ? (n < gc ? n : n - gc) : -1) : (n < gc ? n : -1);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int n = rr;
-          int head;
-          if (kDup) head = (n < 2 * gc) ? (n % gc) : -1;
-          else head = (n < gc) ? n : -1;
           uint32_t v = 0;
           if (head >= 0) {
             const uint32_t addr = sq + head * kD * 2 + (ks * 16 + h * 8 + qd * 2) * 2;
@@ -541,124 +896,130 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         for (int r = 0; r < 4; ++r) acc[md][r] = 0.f;
       m_run[0] = m_run[1] = -INFINITY;
       l_run[0] = l_run[1] = 0.f;
+      const int c0 = 2 * qd, c1 = c0 + 1;
+      mask_hi = (c0 < gc ? 0x0000ffffu : 0u) | (c1 < gc ? 0xffff0000u : 0u);
+      if (kDup) {
+        mask_lo = ((c0 >= gc && c0 < 2 * gc) ? 0x0000ffffu : 0u) |
+                  ((c1 >= gc && c1 < 2 * gc) ? 0xffff0000u : 0u);
+      } else {
+        mask_lo = mask_hi;
+      }
     }
 
-    // ---- S^T = K Q^T: 32 tokens x 8 query columns, FP32 accumulate.
-    float s[2][4];
+    // ---- S^T = K Q^T: TILE tokens x 8 query columns, FP32 accumulate.
+    float s[kMB][4];
 #pragma unroll
-    for (int mb = 0; mb < 2; ++mb) {
+    for (int mb = 0; mb < kMB; ++mb) {
 #pragma unroll
       for (int r = 0; r < 4; ++r) s[mb][r] = 0.f;
-      const int row = mb * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        const int c = ks * 2 + (lane >> 4);
-        const uint32_t addr =
-            sk + (c >> 3) * kHalfBytes + row * 128 + (((c & 7) ^ (lane & 7)) << 4);
         uint32_t a[4];
-        ldsm_x4(addr, a);
+        ldsm_x4(sk + offk[mb] + (ks >> 2) * hs + swzk[ks & 3], a);
         Mma<T>::run(s[mb], a, qf[ks][0], qf[ks][1]);
       }
     }
 
-    // ---- mask, scale, online softmax (split_kv_kernel.py:68-77).
-    const int tb = t.tile * kTile;
-    const bool partial = (t.t0 > tb) || (t.t1 < tb + kTile);
+    // ---- mask, online softmax (split_kv_kernel.py:68-77); scores kept unscaled,
+    // the scale is folded into the exponent.
+    const bool partial = (t0 > tb) || (t1 < tb + TILE);
+    if (partial) {
 #pragma unroll
-    for (int mb = 0; mb < 2; ++mb)
+      for (int mb = 0; mb < kMB; ++mb)
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        float v = s[mb][r] * p.scale_log2;
-        if (partial) {
+        for (int r = 0; r < 4; ++r) {
           const int tok = tb + mb * 16 + rr + (r >> 1) * 8;
-          if (tok < t.t0 || tok >= t.t1) v = -INFINITY;
+          if (tok < t0 || tok >= t1) s[mb][r] = -INFINITY;
         }
-        s[mb][r] = v;
-      }
-    float alpha[2];
+    }
+    float alpha[2], mneg[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      float mx = fmaxf(fmaxf(s[0][e], s[0][e + 2]), fmaxf(s[1][e], s[1][e + 2]));
+      float mx = fmaxf(s[0][e], s[0][e + 2]);
+#pragma unroll
+      for (int mb = 1; mb < kMB; ++mb) mx = fmaxf(mx, fmaxf(s[mb][e], s[mb][e + 2]));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 16));
       const float mn = fmaxf(m_run[e], mx);
-      alpha[e] = exp2f(m_run[e] - mn);
+      alpha[e] = exp2f((m_run[e] - mn) * scl);
       m_run[e] = mn;
+      mneg[e] = -mn * scl;
     }
     float psum[2] = {0.f, 0.f};
 #pragma unroll
-    for (int mb = 0; mb < 2; ++mb)
+    for (int mb = 0; mb < kMB; ++mb)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const float pv = exp2f(s[mb][r] - m_run[r & 1]);
+        const float pv = exp2f(fmaf(s[mb][r], scl, mneg[r & 1]));
         s[mb][r] = pv;
         psum[r & 1] += pv;
       }
+    l_run[0] = fmaf(l_run[0], alpha[0], psum[0]);
+    l_run[1] = fmaf(l_run[1], alpha[1], psum[1]);
+    if (__any_sync(kFull, (alpha[0] != 1.f) || (alpha[1] != 1.f))) {
 #pragma unroll
-    for (int e = 0; e < 2; ++e) l_run[e] = l_run[e] * alpha[e] + psum[e];
-#pragma unroll
-    for (int md = 0; md < 8; ++md) {
-      acc[md][0] *= alpha[0];
-      acc[md][1] *= alpha[1];
-      acc[md][2] *= alpha[0];
-      acc[md][3] *= alpha[1];
+      for (int md = 0; md < 8; ++md) {
+        acc[md][0] *= alpha[0];
+        acc[md][1] *= alpha[1];
+        acc[md][2] *= alpha[0];
+        acc[md][3] *= alpha[1];
+      }
     }
 
-    // ---- P^T as the B operand: hi/lo split keeps ~16 (bf16) / 22 (fp16) bits of p.
-    uint32_t bh[2][2], bl[2][2];
+    // ---- P^T as the B operand; hi + lo keeps ~16 (bf16) / 22 (fp16) bits of p.
+    uint32_t bh[kMB][2], bl[kMB][2];
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
+    for (int kb = 0; kb < kMB; ++kb) {
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        uint16_t hi0, lo0, hi1, lo1;
-        Mma<T>::split(s[kb][half * 2 + 0], hi0, lo0);
-        Mma<T>::split(s[kb][half * 2 + 1], hi1, lo1);
-        const int c0 = qd * 2, c1 = qd * 2 + 1;
+        uint32_t hi, lo;
+        Mma<T>::split2(s[kb][half * 2], s[kb][half * 2 + 1], hi, lo);
         if (kDup) {
-          const uint16_t v0 = c0 < gc ? hi0 : (c0 < 2 * gc ? lo0 : uint16_t(0));
-          const uint16_t v1 = c1 < gc ? hi1 : (c1 < 2 * gc ? lo1 : uint16_t(0));
-          bh[kb][half] = movm_trans(pack16(v0, v1));
+          bh[kb][half] = movm_trans((hi & mask_hi) | (lo & mask_lo));
         } else {
-          bh[kb][half] = movm_trans(pack16(c0 < gc ? hi0 : 0, c1 < gc ? hi1 : 0));
-          bl[kb][half] = movm_trans(pack16(c0 < gc ? lo0 : 0, c1 < gc ? lo1 : 0));
+          bh[kb][half] = movm_trans(hi & mask_hi);
+          bl[kb][half] = movm_trans(lo & mask_lo);
         }
       }
     }
 
     // ---- O^T += V^T P^T (dims x columns).
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
+    for (int kb = 0; kb < kMB; ++kb) {
       uint32_t m01 = 0xffffffffu, m23 = 0xffffffffu;
       if (partial) {
         const int tk = tb + kb * 16 + qd * 2;
-        auto ok = [&](int x) { return x >= t.t0 && x < t.t1; };
-        m01 = (ok(tk) ? 0x0000ffffu : 0u) | (ok(tk + 1) ? 0xffff0000u : 0u);
-        m23 = (ok(tk + 8) ? 0x0000ffffu : 0u) | (ok(tk + 9) ? 0xffff0000u : 0u);
+        m01 = ((tk >= t0 && tk < t1) ? 0x0000ffffu : 0u) |
+              ((tk + 1 >= t0 && tk + 1 < t1) ? 0xffff0000u : 0u);
+        m23 = ((tk + 8 >= t0 && tk + 8 < t1) ? 0x0000ffffu : 0u) |
+              ((tk + 9 >= t0 && tk + 9 < t1) ? 0xffff0000u : 0u);
       }
-      const int row = kb * 16 + (lane >> 4) * 8 + (lane & 7);
 #pragma unroll
       for (int md = 0; md < 8; ++md) {
-        const int c = md * 2 + ((lane >> 3) & 1);
-        const uint32_t addr =
-            sv + (c >> 3) * kHalfBytes + row * 128 + (((c & 7) ^ (lane & 7)) << 4);
         uint32_t a[4];
-        ldsm_x4_t(addr, a);
-        a[0] &= m01;
-        a[1] &= m01;
-        a[2] &= m23;
-        a[3] &= m23;
+        ldsm_x4_t(sv + offv[kb] + (md >> 2) * hs + swzv[md & 3], a);
+        if (partial) {
+          a[0] &= m01;
+          a[1] &= m01;
+          a[2] &= m23;
+          a[3] &= m23;
+        }
         Mma<T>::run(acc[md], a, bh[kb][0], bh[kb][1]);
         if (!kDup) Mma<T>::run(acc[md], a, bl[kb][0], bl[kb][1]);
       }
     }
 
     __syncwarp();
-    if (i + kStages < w.n) issue(i + kStages, st);
+    const int cur = st;
+    st = (st + 1 == NS) ? 0 : st + 1;
+    if (rc >= 0) issue(cur);
 
-    if (!t.last) continue;
+    if (!(fl & 2)) continue;
 
     // ---------------------------------------------------------- piece epilogue
+    const int b = d0.x, kvh = d0.y, qc = d0.z;
+    const int seg_lo = d1.z, seg_hi = d1.w, slot = d2.z;
     float lsum[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -668,7 +1029,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       v += __shfl_xor_sync(kFull, v, 16);
       lsum[e] = v;
     }
-    // Combine hi/lo columns (dup layout): column c + gc holds the low part of c.
+    // Dup layout: column c + gc holds the low part of column c.
     float o[8][4];
 #pragma unroll
     for (int md = 0; md < 8; ++md)
@@ -676,61 +1037,48 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       for (int r = 0; r < 4; ++r) {
         float v = acc[md][r];
         if (kDup) {
-          float partner;
-          if (gc == 1) {
-            partner = acc[md][r | 1];
-          } else {
-            partner = __shfl_down_sync(kFull, v, gc >> 1);
-          }
+          const float partner =
+              (gc == 1) ? acc[md][r | 1] : __shfl_down_sync(kFull, v, gc >> 1);
           v += partner;
         }
         o[md][r] = v;
       }
 
-    // Where this piece's normalised output and LSE go.
-    const bool final_out = (p.ns == 0) && t.whole;
-    long long slot_row = 0;    // split: row of [B*Hq*ns]; balanced: slot
-    int n_pieces = 0, w_first = 0;
-    if (p.ns == 0 && !final_out) {
-      w_first = t.seg_lo / w.per;
-      const int w_last = (t.seg_hi - 1) / w.per;
-      n_pieces = w_last - w_first + 1;
-      const int plo = max(t.seg_lo, w.u0);
-      slot_row = 2ll * wid + (plo == w.u0 ? 0 : 1);
-    }
+    const bool final_out = (p.ns == 0) && (fl & 4);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = qd * 2 + e;
       if (c >= gc) continue;
       const int hq = kvh * G + qc * 8 + c;
-      const float inv_l = 1.f / fmaxf(lsum[e], 1e-20f);
-      const float lse = (m_run[e] + log2f(fmaxf(lsum[e], 1e-20f))) * kLn2;
+      const float lv = fmaxf(lsum[e], 1e-20f);
+      const float inv_l = 1.f / lv;
+      const float lse = (m_run[e] * scl + log2f(lv)) * kLn2;
       if (final_out) {
-        char* dst = p.out + t.b * p.o_sb + hq * p.o_sh;
+        char* dst = p.out + b * p.o_sb + hq * p.o_sh;
 #pragma unroll
         for (int md = 0; md < 8; ++md) {
-          const int d0 = md * 16 + rr;
-          *reinterpret_cast<uint16_t*>(dst + d0 * 2) = Mma<T>::from_float(o[md][e] * inv_l);
-          *reinterpret_cast<uint16_t*>(dst + (d0 + 8) * 2) =
+          const int d0i = md * 16 + rr;
+          *reinterpret_cast<uint16_t*>(dst + d0i * 2) = Mma<T>::from_float(o[md][e] * inv_l);
+          *reinterpret_cast<uint16_t*>(dst + (d0i + 8) * 2) =
               Mma<T>::from_float(o[md][e + 2] * inv_l);
         }
-        if (rr == 0 && p.lse) p.lse[t.b * p.Hq + hq] = lse;
+        if (rr == 0 && p.lse) p.lse[b * p.Hq + hq] = lse;
       } else {
         float* od;
         float* ld;
         if (p.ns == 0) {
-          od = p.o_part + (slot_row * 8 + c) * kD;
-          ld = p.lse_part + slot_row * 8 + c;
+          od = p.o_part + (static_cast<long long>(slot) * p.slot_cols + c) * kD;
+          ld = p.lse_part + static_cast<long long>(slot) * p.slot_cols + c;
         } else {
-          const long long row = (static_cast<long long>(t.b) * p.Hq + hq) * p.ns + t.seg_lo;
+          const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + slot;
           od = p.o_part + row * kD;
           ld = p.lse_part + row;
         }
 #pragma unroll
         for (int md = 0; md < 8; ++md) {
-          const int d0 = md * 16 + rr;
-          od[d0] = o[md][e] * inv_l;
-          od[d0 + 8] = o[md][e + 2] * inv_l;
+          const int d0i = md * 16 + rr;
+          od[d0i] = o[md][e] * inv_l;
+          od[d0i + 8] = o[md][e + 2] * inv_l;
         }
         if (rr == 0) *ld = lse;
       }
@@ -740,109 +1088,38 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     // Publish the partial; the last arriving piece merges the segment.
     __threadfence();
     __syncwarp();
-    const int n_expect = (p.ns == 0) ? n_pieces : p.ns;
-    const int cid = (t.b * p.Hkv + kvh) * p.QC + qc;
+    PieceSet ps;
+    ps.n = 0;
+    if (p.ns == 0) ps = pieces_of(p, sc, seg_lo, seg_hi);
+    const int n_expect = (p.ns == 0) ? ps.n : p.ns;
+    const int cid = (b * p.Hkv + kvh) * p.QC + qc;
     int last = 0;
     if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == n_expect - 1);
     last = __shfl_sync(kFull, last, 0);
     if (!last) continue;
     __threadfence();
-
-    // ------------------------------------------------------ merge (last arriver)
-    // split_kv_kernel.py:101-122: skip lse <= -1e29, running max, divide by
-    // max(sum, 1e-20). Each lane owns 4 dims.
-    for (int j = 0; j < gc; ++j) {
-      const int hq = kvh * G + qc * 8 + j;
-      auto part = [&](int k, const float*& op, const float*& lp) {
-        if (p.ns == 0) {
-          const int wk = w_first + k;
-          const int plo = max(t.seg_lo, wk * w.per);
-          const long long sl = 2ll * wk + (plo == wk * w.per ? 0 : 1);
-          op = p.o_part + (sl * 8 + j) * kD;
-          lp = p.lse_part + sl * 8 + j;
-        } else {
-          const long long row = (static_cast<long long>(t.b) * p.Hq + hq) * p.ns + k;
-          op = p.o_part + row * kD;
-          lp = p.lse_part + row;
-        }
-      };
-      float gmax = kValidLse;
-      for (int k = lane; k < n_expect; k += 32) {
-        const float* op;
-        const float* lp;
-        part(k, op, lp);
-        const float l = __ldcg(lp);
-        if (l > kValidLse) gmax = fmaxf(gmax, l);
-      }
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
-      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      float gsum = 0.f;
-      for (int k = 0; k < n_expect; ++k) {
-        const float* op;
-        const float* lp;
-        part(k, op, lp);
-        const float l = __ldcg(lp);
-        if (!(l > kValidLse)) continue;
-        const float wgt = exp2f((l - gmax) * kLog2e);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(op) + lane);
-        a4.x += wgt * v.x;
-        a4.y += wgt * v.y;
-        a4.z += wgt * v.z;
-        a4.w += wgt * v.w;
-        gsum += wgt;
-      }
-      const float inv = 1.f / fmaxf(gsum, 1e-20f);
-      char* dst = p.out + t.b * p.o_sb + hq * p.o_sh + lane * 8;
-      const uint32_t lo = pack16(Mma<T>::from_float(a4.x * inv), Mma<T>::from_float(a4.y * inv));
-      const uint32_t hi = pack16(Mma<T>::from_float(a4.z * inv), Mma<T>::from_float(a4.w * inv));
-      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-      if (lane == 0 && p.lse)
-        p.lse[t.b * p.Hq + hq] = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
-    }
+    merge_segment<T>(p, sc, b, kvh, qc, gc, ps, lane);
     if (lane == 0) atomicExch(p.counters + cid, 0);
   }
 
-  // Split schedule, empty piece that arrived last: merge with no tiles of its own.
-  if (p.ns != 0 && w.n == 0) {
-    int kvh, qc, gc;
-    seg_heads(w.seg, kvh, qc, gc);
-    for (int j = 0; j < gc; ++j) {
-      const int hq = kvh * G + qc * 8 + j;
-      const long long row0 = (static_cast<long long>(w.b) * p.Hq + hq) * p.ns;
-      float gmax = kValidLse;
-      for (int k = lane; k < p.ns; k += 32) {
-        const float l = __ldcg(p.lse_part + row0 + k);
-        if (l > kValidLse) gmax = fmaxf(gmax, l);
-      }
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
-      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-      float gsum = 0.f;
-      for (int k = 0; k < p.ns; ++k) {
-        const float l = __ldcg(p.lse_part + row0 + k);
-        if (!(l > kValidLse)) continue;
-        const float wgt = exp2f((l - gmax) * kLog2e);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(p.o_part + (row0 + k) * kD) + lane);
-        a4.x += wgt * v.x;
-        a4.y += wgt * v.y;
-        a4.z += wgt * v.z;
-        a4.w += wgt * v.w;
-        gsum += wgt;
-      }
-      const float inv = 1.f / fmaxf(gsum, 1e-20f);
-      char* dst = p.out + w.b * p.o_sb + hq * p.o_sh + lane * 8;
-      const uint32_t lo = pack16(Mma<T>::from_float(a4.x * inv), Mma<T>::from_float(a4.y * inv));
-      const uint32_t hi = pack16(Mma<T>::from_float(a4.z * inv), Mma<T>::from_float(a4.w * inv));
-      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-      if (lane == 0 && p.lse)
-        p.lse[w.b * p.Hq + hq] = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
-    }
-    if (lane == 0) atomicExch(p.counters + (w.b * p.Hkv + kvh) * p.QC + qc, 0);
+  if (merge_empty) {
+    const int gc = min(8, G - w.qc * 8);
+    PieceSet ps;
+    ps.n = 0;
+    merge_segment<T>(p, sc, w.b, w.kvh, w.qc, gc, ps, lane);
+    if (lane == 0) atomicExch(p.counters + (w.b * p.Hkv + w.kvh) * p.QC + w.qc, 0);
   }
-  (void)aborted;
+
+  // Dynamic ranges: the last worker to finish rewinds the range counter.
+  if (p.ns == 0 && sc.nd > 0 && !aborted && lane == 0) {
+    if (atomicAdd(sched_ctr + 1, 1) == p.W - 1) {
+      atomicExch(sched_ctr, 0);
+      atomicExch(sched_ctr + 1, 0);
+    }
+  }
 }
 
+// ----------------------------------------------------------------------------
 // ----------------------------------------------------------------------------
 // Bandwidth probes (replace measure_peak_bw.py:15-21's Triton copy kernel)
 // ----------------------------------------------------------------------------
@@ -894,7 +1171,6 @@ __global__ void __launch_bounds__(512) stream_read_kernel(const uint4* __restric
 // ----------------------------------------------------------------------------
 struct DeviceInfo {
   int sms = 0;
-  bool attr_set[4] = {false, false, false, false};
 };
 
 static std::mutex g_mu;
@@ -940,13 +1216,34 @@ static int gcd_int(int a, int b) {
   return a;
 }
 
+// Kernel variants: tile tokens, worker warps per CTA, ring depth per warp.
+struct Variant {
+  int tile, nw, ns;
+};
+static const Variant kVariants[] = {
+    {32, 4, 3},   // 1
+    {16, 8, 3},   // 2 (dup layout only: 9 KB stages)
+    {32, 6, 2},   // 3
+    {16, 12, 2},  // 4 (dup layout only)
+    {16, 8, 2},   // 5
+};
+constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+constexpr int kStaticPct = 80;      // balanced: units in static per-worker ranges
+constexpr int kDynPerWorker = 3;    // balanced: dynamic ranges per worker (bound)
+constexpr int kHybridMinUnits = 1 << 20;  // balanced: static only up to this many units per worker
+constexpr int kMinDynUnits = 4;     // balanced: smallest dynamic range
+
 struct Plan {
   int ns = 0;        // 0: balanced
   int grid = 0;
   int W = 0;
   int G = 1, QC = 1;
+  bool dup = true;
+  int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
+  int slot_cols = 1;
   size_t ws_bytes = 0;
+  size_t seg_counters = 0;
   size_t counters = 0;
 };
 
@@ -958,23 +1255,39 @@ static pa_status_t validate(const pa_decode_params* p) {
   if (p->num_heads % p->num_kv_heads != 0) return PA_ERR_ARG;
   if (p->dtype != PA_F16 && p->dtype != PA_BF16) return PA_ERR_ARG;
   if (p->num_splits < 0) return PA_ERR_ARG;
+  if (!(p->scale > 0.f) || p->scale > 1e30f) return PA_ERR_ARG;
   if (p->seq_lens == nullptr && p->seq_len < 0) return PA_ERR_ARG;
   if (p->seq_lens == nullptr && static_cast<long long>(p->seq_len) >
                                     static_cast<long long>(p->max_blocks) * p->block_size)
     return PA_ERR_ARG;
+  if (p->kernel_variant < 0 || p->kernel_variant > kNumVariants) return PA_ERR_ARG;
   if (p->head_dim != kD) return PA_ERR_UNSUPPORTED;
   if (p->block_size % 8 != 0 || p->block_size > (1 << 20)) return PA_ERR_UNSUPPORTED;
   return PA_OK;
 }
 
+// Automatic choice, from B200 sweeps of the five benchmark shapes: pages
+// shorter than 32 tokens stream best as 16-token tiles on 8 warps (one page per
+// box, two boxes per K/V tile would double the copies); longer pages as
+// 32-token tiles on 6 warps.
+static int pick_variant(const pa_decode_params* p, bool dup) {
+  int v = p->kernel_variant;
+  if (v == 0) v = (p->block_size < 32) ? 5 : 3;
+  if (!dup && (v == 2 || v == 4)) v = 5;
+  return v;
+}
+
 static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
   pl.G = p->num_heads / p->num_kv_heads;
   pl.QC = (pl.G + 7) / 8;
+  pl.dup = (pl.G == 1 || pl.G == 2 || pl.G == 4);
+  pl.variant = pick_variant(p, pl.dup);
+  const Variant& v = kVariants[pl.variant - 1];
   const long long nseg = static_cast<long long>(p->num_kv_heads) * pl.QC;
   const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
   pl.ns = p->num_splits;
   if (pl.ns == 0) {
-    const long long nt = (cap + kTile - 1) / kTile;
+    const long long nt = (cap + v.tile - 1) / v.tile;
     // Unit indices must fit int32; very large batches with per-row lengths
     // use the split schedule with the reference heuristic instead.
     if ((p->seq_lens != nullptr && p->batch > kCumMax) ||
@@ -983,58 +1296,107 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
       pl.ns = pa_num_splits_heuristic(p->batch, p->num_heads, s_max, p->block_size, sms);
     }
   }
+  pl.slot_cols = std::min(pl.G, 8);
   if (pl.ns == 0) {
     pl.grid = sms;
-    pl.W = pl.grid * kWarps;
+    pl.W = pl.grid * v.nw;
     pl.use_cum = p->seq_lens != nullptr;
-    pl.ws_bytes = static_cast<size_t>(2) * pl.W * 8 * (kD + 1) * sizeof(float);
+    const size_t slots = static_cast<size_t>(2) * pl.W * (1 + kDynPerWorker);
+    pl.ws_bytes = slots * pl.slot_cols * (kD + 1) * sizeof(float);
   } else {
     const long long workers = static_cast<long long>(p->batch) * nseg * pl.ns;
     if (workers > 0x7fffffffll) return PA_ERR_UNSUPPORTED;
     pl.W = static_cast<int>(workers);
-    pl.grid = static_cast<int>((workers + kWarps - 1) / kWarps);
+    pl.grid = static_cast<int>((workers + v.nw - 1) / v.nw);
     const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
     pl.ws_bytes = (p->o_partial && p->lse_partial) ? 0 : rows * (kD + 1) * sizeof(float);
   }
-  pl.counters = static_cast<size_t>(p->batch) * nseg;
+  pl.seg_counters = static_cast<size_t>(p->batch) * nseg;
+  pl.counters = pl.seg_counters + 2;   // + dynamic-range counter and done counter
   return PA_OK;
 }
 
+// Tensor map of one paged cache [num_blocks, block_size, Hkv, 128]. The 5-D
+// form orders the dimensions (64 dims, slot, dim-half, head, block) so that one
+// box of {64, R, 2, 1, 1} lands as [half][R rows][128 B]: both halves of R token
+// rows in one copy. The 4-D form {128 dims, head, slot, block} with box
+// {64, 1, R, 1} needs one copy per half.
 static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const void* base,
-                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows) {
+                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows,
+                             bool five_d) {
   auto fn = encode_fn();
   if (!fn) return false;
   const CUtensorMapDataType dt =
       p->dtype == PA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(p->num_kv_heads),
-                        static_cast<cuuint64_t>(p->block_size),
-                        static_cast<cuuint64_t>(p->num_blocks)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2, static_cast<cuuint64_t>(s_slot) * 2,
-                           static_cast<cuuint64_t>(s_block) * 2};
-  cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (five_d) {
+    cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(p->block_size), 2,
+                          static_cast<cuuint64_t>(p->num_kv_heads),
+                          static_cast<cuuint64_t>(p->num_blocks)};
+    cuuint64_t strides[4] = {static_cast<cuuint64_t>(s_slot) * 2, 128,
+                             static_cast<cuuint64_t>(s_head) * 2,
+                             static_cast<cuuint64_t>(s_block) * 2};
+    cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows), 2, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    r = fn(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(p->num_kv_heads),
+                          static_cast<cuuint64_t>(p->block_size),
+                          static_cast<cuuint64_t>(p->num_blocks)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2,
+                             static_cast<cuuint64_t>(s_slot) * 2,
+                             static_cast<cuuint64_t>(s_block) * 2};
+    cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   return r == CUDA_SUCCESS;
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
-template <typename T, bool kDup>
-static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
-                          const KParams& kp, cudaStream_t stream, int dev, int attr_idx) {
+template <typename T, bool kDup, int TILE, int NW, int NS>
+static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
+                              const KParams& kp, cudaStream_t stream, int dev) {
+  using C = Cfg<kDup, TILE, NW, NS>;
+  static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
+  static bool attr_set[64] = {false};
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_dev[dev].attr_set[attr_idx]) {
-      const cudaError_t e = cudaFuncSetAttribute(
-          pa_decode_kernel<T, kDup>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (!attr_set[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::kSmem);
       if (e != cudaSuccess) return e;
-      g_dev[dev].attr_set[attr_idx] = true;
+      attr_set[dev] = true;
     }
   }
-  pa_decode_kernel<T, kDup><<<pl.grid, kWarps * 32, kSmemBytes, stream>>>(mk, mv, kp);
+  pa_decode_kernel<T, kDup, TILE, NW, NS><<<pl.grid, NW * 32, C::kSmem, stream>>>(mk, mv, kp);
   return cudaGetLastError();
+}
+
+template <typename T, bool kDup>
+static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
+                          const KParams& kp, cudaStream_t stream, int dev) {
+  switch (pl.variant) {
+    case 2:
+      if constexpr (kDup) return launch_one<T, kDup, 16, 8, 3>(pl, mk, mv, kp, stream, dev);
+      break;
+    case 3:
+      return launch_one<T, kDup, 32, 6, 2>(pl, mk, mv, kp, stream, dev);
+    case 4:
+      if constexpr (kDup) return launch_one<T, kDup, 16, 12, 2>(pl, mk, mv, kp, stream, dev);
+      break;
+    case 5:
+      return launch_one<T, kDup, 16, 8, 2>(pl, mk, mv, kp, stream, dev);
+    default:
+      break;
+  }
+  return launch_one<T, kDup, 32, 4, 3>(pl, mk, mv, kp, stream, dev);
 }
 
 }  // namespace pa
@@ -1125,13 +1487,13 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.QC = pl.QC;
   kp.bs = p->block_size;
   kp.NB = p->num_blocks;
-  kp.nseg = p->num_kv_heads * pl.QC;
   kp.ns = pl.ns;
   kp.scale_log2 = p->scale * kLog2e;
   if (pl.ns == 0) {
     float* ws = static_cast<float*>(p->workspace);
+    const size_t slots = static_cast<size_t>(2) * pl.W * (1 + kDynPerWorker);
     kp.o_part = ws;
-    kp.lse_part = ws + static_cast<size_t>(2) * pl.W * 8 * kD;
+    kp.lse_part = ws + slots * pl.slot_cols * kD;
   } else if (p->o_partial && p->lse_partial) {
     kp.o_part = p->o_partial;
     kp.lse_part = p->lse_partial;
@@ -1143,26 +1505,45 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   }
   kp.counters = p->counters;
   kp.status = p->status;
-  kp.R = gcd_int(p->block_size, kTile);
-  kp.spt = kTile / kp.R;
+  const int tile = kVariants[pl.variant - 1].tile;
+  kp.R = gcd_int(p->block_size, tile);
+  kp.lspt = 0;
+  while ((kp.R << kp.lspt) < tile) ++kp.lspt;
+  kp.lR = 0;
+  while ((1 << kp.lR) < kp.R) ++kp.lR;
+  kp.bs_log2 = -1;
+  for (int k = 0; k < 31; ++k)
+    if ((1 << k) == p->block_size) kp.bs_log2 = k;
   kp.W = pl.W;
   kp.use_cum = pl.use_cum ? 1 : 0;
+  kp.slot_cols = pl.slot_cols;
+  kp.static_pct = kStaticPct;
+  kp.dyn_per_worker = kDynPerWorker;
+  kp.n_seg_counters = static_cast<int>(pl.seg_counters);
+  kp.hybrid_min_units = kHybridMinUnits;
+  kp.min_dyn_units = kMinDynUnits;
 
   CUtensorMap mk, mv;
+  kp.map5d = 1;
   if (!encode_cache_map(&mk, p, p->k_cache, p->k_stride_block, p->k_stride_slot, p->k_stride_head,
-                        kp.R) ||
+                        kp.R, true) ||
       !encode_cache_map(&mv, p, p->v_cache, p->v_stride_block, p->v_stride_slot, p->v_stride_head,
-                        kp.R))
-    return PA_ERR_ARG;
+                        kp.R, true)) {
+    kp.map5d = 0;
+    if (!encode_cache_map(&mk, p, p->k_cache, p->k_stride_block, p->k_stride_slot,
+                          p->k_stride_head, kp.R, false) ||
+        !encode_cache_map(&mv, p, p->v_cache, p->v_stride_block, p->v_stride_slot,
+                          p->v_stride_head, kp.R, false))
+      return PA_ERR_ARG;
+  }
 
-  const bool dup = (pl.G == 1 || pl.G == 2 || pl.G == 4);
   cudaError_t e;
   if (p->dtype == PA_F16)
-    e = dup ? launch<__half, true>(pl, mk, mv, kp, stream, dev, 0)
-            : launch<__half, false>(pl, mk, mv, kp, stream, dev, 1);
+    e = pl.dup ? launch<__half, true>(pl, mk, mv, kp, stream, dev)
+               : launch<__half, false>(pl, mk, mv, kp, stream, dev);
   else
-    e = dup ? launch<__nv_bfloat16, true>(pl, mk, mv, kp, stream, dev, 2)
-            : launch<__nv_bfloat16, false>(pl, mk, mv, kp, stream, dev, 3);
+    e = pl.dup ? launch<__nv_bfloat16, true>(pl, mk, mv, kp, stream, dev)
+               : launch<__nv_bfloat16, false>(pl, mk, mv, kp, stream, dev);
   return e == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

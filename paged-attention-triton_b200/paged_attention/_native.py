@@ -66,6 +66,7 @@ class DecodeParams(ctypes.Structure):
         ("counters", ctypes.c_void_p),
         ("counter_count", ctypes.c_size_t),
         ("status", ctypes.c_void_p),
+        ("kernel_variant", ctypes.c_int32),
     ]
 
 

@@ -128,7 +128,8 @@ def _decode(Q: torch.Tensor, K_Cache: torch.Tensor, V_Cache: torch.Tensor,
             Block_Table: torch.Tensor, seq_len: Union[int, torch.Tensor], block_size: int,
             num_splits: Optional[int] = None, scale: Optional[float] = None,
             return_lse: bool = False, return_partials: bool = False,
-            workspace: Optional[DecodeWorkspace] = None, out: Optional[torch.Tensor] = None):
+            workspace: Optional[DecodeWorkspace] = None, out: Optional[torch.Tensor] = None,
+            kernel_variant: int = 0):
     _check(Q.is_cuda and K_Cache.is_cuda and V_Cache.is_cuda and Block_Table.is_cuda,
            "paged_attention: Q, K_Cache, V_Cache and Block_Table must be CUDA tensors")
     _check(Q.dim() == 3, "paged_attention: Q must be [B, H, D]")
@@ -206,6 +207,7 @@ def _decode(Q: torch.Tensor, K_Cache: torch.Tensor, V_Cache: torch.Tensor,
     p.lse = lse.data_ptr() if lse is not None else None
     p.o_partial = o_part.data_ptr() if o_part is not None else None
     p.lse_partial = lse_part.data_ptr() if lse_part is not None else None
+    p.kernel_variant = int(kernel_variant)
 
     lib = _native.lib()
     ws_bytes = ctypes.c_size_t(0)
@@ -251,10 +253,13 @@ class PagedAttentionV2Function(torch.autograd.Function):
 
 
 def paged_attention(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_splits=None, *,
-                    scale=None, return_lse=False, return_partials=False, workspace=None, out=None):
+                    scale=None, return_lse=False, return_partials=False, workspace=None, out=None,
+                    kernel_variant=0):
     """Decode attention of one new token per sequence over a paged KV cache.
 
     Reference signature: ``paged_attention/torch_kernel.py:71-73``.
+    ``kernel_variant`` (0 = automatic) pins one tile/warp/stage variant of the
+    CUDA kernel; it exists for tuning and tests.
     """
     if torch.is_grad_enabled() and (Q.requires_grad or K_Cache.requires_grad
                                     or V_Cache.requires_grad):
@@ -263,4 +268,4 @@ def paged_attention(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_s
                                                   block_size, num_splits)
         raise RuntimeError("PagedAttentionV2 is inference-only.")
     return _decode(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_splits, scale,
-                   return_lse, return_partials, workspace, out)
+                   return_lse, return_partials, workspace, out, kernel_variant)

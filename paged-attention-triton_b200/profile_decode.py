@@ -1,0 +1,61 @@
+"""Launch the decode kernel a few times on one benchmark shape, for profilers.
+
+    python profile_decode.py --config c2 [--iters 3] [--num-splits 0] [--flush]
+
+Builds the seeded workload, runs one warm-up launch and ``--iters`` timed
+launches (L2 flushed before each with ``--flush``) and prints the mean device
+time and effective GB/s. Meant to be wrapped by ``ncu`` with ``-k
+regex:pa_decode_kernel -s 1 -c <iters>``; small enough for full-metric
+captures (c2 holds ~1.1 GB of KV on the device).
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+import paged_attention as pa  # noqa: E402
+from paged_attention import workloads  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default="c2", choices=sorted(workloads.CONFIGS))
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--num-splits", type=int, default=0)
+    ap.add_argument("--flush", action="store_true")
+    ap.add_argument("--variant", type=int, default=0, help="kernel variant (0 = automatic)")
+    a = ap.parse_args()
+    w = workloads.CONFIGS[a.config]("cuda")
+    ws = pa.DecodeWorkspace("cuda")
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if a.flush else None
+
+    def op():
+        return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                  w.block_size, a.num_splits, workspace=ws,
+                                  kernel_variant=a.variant)
+
+    op()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(a.iters):
+        if flush is not None:
+            flush.fill_(1)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        op()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    ms = sum(times) / len(times)
+    print(f"{w.name} variant {a.variant}: {ms * 1e3:.1f} us/launch, {w.effective_bytes() / ms / 1e6:.1f} GB/s, "
+          f"status={ws.read_status()}")
+
+
+if __name__ == "__main__":
+    main()

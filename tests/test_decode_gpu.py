@@ -166,6 +166,35 @@ def test_sweep_block_size_group(pa, oracle, dtype, bs, group):
     _check_workload(pa, oracle, w, num_splits=3)
 
 
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("group,bs,dtype", [(1, 16, torch.float16), (4, 24, torch.bfloat16),
+                                            (8, 128, torch.bfloat16), (3, 8, torch.float16)])
+def test_kernel_variants(pa, oracle, variant, group, bs, dtype):
+    """Every tile/warp/stage variant, both schedules, against the oracle."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(variant * 10 + group)
+    b, hkv = 7, 2
+    lens = torch.randint(0, 400, (b,), generator=g, dtype=torch.int32)
+    lens[2] = 0
+    max_blocks = (400 + bs - 1) // bs
+    w = workloads.build("variant", b, hkv * group, hkv, bs, dtype, lens.cuda(), max_blocks,
+                        b * max_blocks, seed=variant, device="cuda")
+    ro, rl = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs)
+    for ns in (None, 5):
+        ws = pa.DecodeWorkspace("cuda")
+        o, lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len, bs, ns,
+                                    return_lse=True, workspace=ws, kernel_variant=variant)
+        torch.cuda.synchronize()
+        assert ws.read_status() == 0
+        assert_o_close(o, ro, f"variant {variant} ns={ns}")
+        assert_lse_close(lse, rl, f"variant {variant} ns={ns} LSE")
+    # uniform-length path of the balanced schedule
+    o = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, 300, bs,
+                           kernel_variant=variant)
+    ro2, _ = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, 300, bs)
+    assert_o_close(o, ro2, f"variant {variant} uniform")
+
+
 # --------------------------------------------------------------------------- KATs
 def test_kat_single_token_bit_exact(pa):
     """S=1: the softmax weight is exactly 1, so O equals the V row bit-exactly
