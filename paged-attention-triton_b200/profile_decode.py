@@ -32,7 +32,13 @@ def main():
     a = ap.parse_args()
     w = workloads.CONFIGS[a.config]("cuda")
     ws = pa.DecodeWorkspace("cuda")
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if a.flush else None
+    wbuf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if a.flush else None
+    rbuf = torch.ones(128 << 20, dtype=torch.int32, device="cuda") if a.flush else None
+
+    def flush():
+        # evict L2 by writing 512 MB, then read 512 MB so no dirty lines remain
+        wbuf.fill_(1)
+        rbuf.sum(dtype=torch.int64)
 
     def op():
         return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
@@ -43,8 +49,8 @@ def main():
     torch.cuda.synchronize()
     times = []
     for _ in range(a.iters):
-        if flush is not None:
-            flush.fill_(1)
+        if wbuf is not None:
+            flush()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
