@@ -627,7 +627,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   if (p.ns == 0) {
     const int W = p.W;
     sc.U = p.use_cum ? cum[p.B] : p.B * p.Hkv * p.QC * ((p.seq_len + TILE - 1) / TILE);
-    if (sc.U <= p.hybrid_min_units * W) {
+    if (static_cast<long long>(sc.U) <= static_cast<long long>(p.hybrid_min_units) * W) {
       // small step: static ranges only (dynamic ranges would cost more than the tail)
       sc.Ps = max(1, (sc.U + W - 1) / W);
       sc.Us = sc.U;
@@ -1242,10 +1242,17 @@ struct Plan {
   int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
   int slot_cols = 1;
+  bool dyn_slots = false;  // balanced: room for dynamic-range partials
   size_t ws_bytes = 0;
   size_t seg_counters = 0;
   size_t counters = 0;
 };
+
+// Partial slots of the balanced schedule: two per static range, plus two per
+// dynamic range when the hybrid schedule can occur.
+static size_t plan_slots(const Plan& pl) {
+  return static_cast<size_t>(2) * pl.W * (1 + (pl.dyn_slots ? kDynPerWorker : 0));
+}
 
 static pa_status_t validate(const pa_decode_params* p) {
   if (!p) return PA_ERR_ARG;
@@ -1301,8 +1308,12 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     pl.grid = sms;
     pl.W = pl.grid * v.nw;
     pl.use_cum = p->seq_lens != nullptr;
-    const size_t slots = static_cast<size_t>(2) * pl.W * (1 + kDynPerWorker);
-    pl.ws_bytes = slots * pl.slot_cols * (kD + 1) * sizeof(float);
+    // Dynamic ranges exist only when a step can exceed kHybridMinUnits units
+    // per worker; otherwise only the 2W static slots are ever written.
+    const long long u_max = static_cast<long long>(p->batch) * nseg *
+                            ((cap + v.tile - 1) / v.tile);
+    pl.dyn_slots = u_max > static_cast<long long>(kHybridMinUnits) * pl.W;
+    pl.ws_bytes = plan_slots(pl) * pl.slot_cols * (kD + 1) * sizeof(float);
   } else {
     const long long workers = static_cast<long long>(p->batch) * nseg * pl.ns;
     if (workers > 0x7fffffffll) return PA_ERR_UNSUPPORTED;
@@ -1491,9 +1502,8 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.scale_log2 = p->scale * kLog2e;
   if (pl.ns == 0) {
     float* ws = static_cast<float*>(p->workspace);
-    const size_t slots = static_cast<size_t>(2) * pl.W * (1 + kDynPerWorker);
     kp.o_part = ws;
-    kp.lse_part = ws + slots * pl.slot_cols * kD;
+    kp.lse_part = ws + plan_slots(pl) * pl.slot_cols * kD;
   } else if (p->o_partial && p->lse_partial) {
     kp.o_part = p->o_partial;
     kp.lse_part = p->lse_partial;
@@ -1520,7 +1530,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.static_pct = kStaticPct;
   kp.dyn_per_worker = kDynPerWorker;
   kp.n_seg_counters = static_cast<int>(pl.seg_counters);
-  kp.hybrid_min_units = kHybridMinUnits;
+  kp.hybrid_min_units = pl.dyn_slots ? kHybridMinUnits : INT_MAX;
   kp.min_dyn_units = kMinDynUnits;
 
   CUtensorMap mk, mv;
