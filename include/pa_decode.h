@@ -109,6 +109,33 @@ PA_API pa_status_t pa_decode_workspace(const pa_decode_params* p, size_t* worksp
 /* Launch one decode step on `stream` (one kernel). */
 PA_API pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream);
 
+/* Allocation-free variant of pa_decode. It has no counterpart in the reference.
+ *
+ * pa_decode needs scratch memory (partial outputs of split segments and the
+ * arrival counters) that the caller allocates. Some callers cannot allocate
+ * device memory: a plugin or operator host that hands a kernel only its
+ * input and output buffers, a runtime whose device memory is carved up once at
+ * start-up with no allocator reachable afterwards, or a C caller without
+ * access to a device allocator. pa_decode_noalloc takes the same parameters,
+ * ignores `workspace`, `workspace_bytes`, `counters` and `counter_count`, and
+ * uses a fixed scratch array that the library itself holds in device memory:
+ *
+ *  - The array is PA_NOALLOC_SCRATCH_BYTES (16 MiB) and every GPU that loads
+ *    the library keeps it until the process exits. A call whose scratch
+ *    (partials + counters, as pa_decode_workspace reports) does not fit is
+ *    rejected with PA_ERR_WORKSPACE, before anything is launched.
+ *  - The first call on each device looks up the array's device address once
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture.
+ *  - Every call on a device shares the one array, and the array keeps the
+ *    last call's contents. Each call clears the counter part (an async memset
+ *    on `stream`) before its kernel. Calls whose executions overlap on the GPU
+ *    (different streams without ordering between them) race on the array and
+ *    give wrong results; order them on one stream.
+ *  - It calls no cudaMalloc, cudaFree or other allocating routine. */
+#define PA_NOALLOC_SCRATCH_BYTES (16u << 20)
+PA_API pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t stream);
+
 /* max(1, min(ceil(S / block_size), max(1, 4 * sm_count / (batch * heads)))). */
 PA_API int32_t pa_num_splits_heuristic(int32_t batch, int32_t heads, int32_t seq_len,
                                 int32_t block_size, int32_t sm_count);

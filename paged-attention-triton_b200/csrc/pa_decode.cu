@@ -1557,6 +1557,58 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   return e == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
+}  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Allocation-free entry point: scratch in a file-scope device array
+// ----------------------------------------------------------------------------
+namespace pa {
+
+// Zero-initialised at module load on every device that loads the library.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PA_NOALLOC_SCRATCH_BYTES];
+static void* g_noalloc_addr[64];   // device address of g_noalloc_scratch, per device
+
+// Device address of the scratch array on `dev` (the current device); looked
+// up once per device. The host-side symbol is not a device address.
+static void* noalloc_scratch(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_noalloc_addr[dev] = ptr;
+  }
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace pa
+
+extern "C" {
+
+pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t stream) {
+  const pa_status_t v = validate(p);
+  if (v != PA_OK) return v;
+  const int dev = current_device();
+  const int sms = sm_count(dev);
+  if (sms <= 0) return PA_ERR_LAUNCH;
+  Plan pl;
+  const pa_status_t s = make_plan(p, sms, pl);
+  if (s != PA_OK) return s;
+  const size_t counter_bytes = (pl.counters * sizeof(int32_t) + 255) & ~size_t(255);
+  if (counter_bytes + pl.ws_bytes > PA_NOALLOC_SCRATCH_BYTES) return PA_ERR_WORKSPACE;
+  if (p->batch == 0) return pa_decode(p, stream);
+  unsigned char* base = static_cast<unsigned char*>(noalloc_scratch(dev));
+  if (!base) return PA_ERR_LAUNCH;
+  // The counters must start at zero; the previous call's partials need no clearing.
+  if (cudaMemsetAsync(base, 0, counter_bytes, stream) != cudaSuccess) return PA_ERR_LAUNCH;
+  pa_decode_params q = *p;
+  q.counters = reinterpret_cast<int32_t*>(base);
+  q.counter_count = pl.counters;
+  q.workspace = pl.ws_bytes ? base + counter_bytes : nullptr;
+  q.workspace_bytes = pl.ws_bytes;
+  return pa_decode(&q, stream);
+}
+
 pa_status_t pa_stream_copy(const void* src, void* dst, size_t bytes, cudaStream_t stream) {
   if (!src || !dst || (bytes & 15) || !aligned16(src) || !aligned16(dst)) return PA_ERR_ARG;
   const int sms = sm_count(current_device());

@@ -25,6 +25,9 @@ PA_STATUS_BAD_BLOCK = 1
 PA_STATUS_BAD_SEQLEN = 2
 PA_STATUS_TIMEOUT = 4
 
+# size of the scratch array pa_decode_noalloc uses (PA_NOALLOC_SCRATCH_BYTES)
+PA_NOALLOC_SCRATCH_BYTES = 16 << 20
+
 
 class DecodeParams(ctypes.Structure):
     """Mirror of ``pa_decode_params`` (field order and types must match)."""
@@ -76,6 +79,7 @@ _SIGNATURES = {
                                            ctypes.POINTER(ctypes.c_size_t),
                                            ctypes.POINTER(ctypes.c_size_t)]),
     "pa_decode": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
+    "pa_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
     "pa_num_splits_heuristic": (ctypes.c_int32, [ctypes.c_int32] * 5),
     "pa_stream_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.c_void_p]),

@@ -1,0 +1,104 @@
+"""GPU test of pa_decode_noalloc, the allocation-free entry point.
+
+Callers that cannot allocate device memory (a plugin host that only hands over
+input and output buffers, a runtime whose memory is carved up once at start-up)
+use pa_decode_noalloc: the library's own fixed scratch array replaces the
+caller's workspace and counters. These tests call it through the C ABI and
+check its output against pa_decode (through the package's public entry point)
+on two calls in a row, within the tolerances the other GPU tests use. The file
+is collected last so that a run stopping at the first failure has already run
+every other test; it also passes alone in a fresh process, where its first call
+performs the one-time per-device set-up.
+"""
+import ctypes
+import math
+
+import pytest
+import torch
+
+from helpers import assert_lse_close, assert_o_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _params(q, k, v, bt, seq, bs, out, lse, num_splits=0):
+    from paged_attention import _native
+    p = _native.DecodeParams()
+    p.q = q.data_ptr()
+    p.q_stride_b, p.q_stride_h = q.stride(0), q.stride(1)
+    p.k_cache = k.data_ptr()
+    p.k_stride_block, p.k_stride_slot, p.k_stride_head = k.stride(0), k.stride(1), k.stride(2)
+    p.v_cache = v.data_ptr()
+    p.v_stride_block, p.v_stride_slot, p.v_stride_head = v.stride(0), v.stride(1), v.stride(2)
+    p.block_table = bt.data_ptr()
+    p.bt_stride_b = bt.stride(0)
+    p.max_blocks = bt.shape[1]
+    if isinstance(seq, torch.Tensor):
+        p.seq_lens = seq.data_ptr()
+        p.seq_len = 0
+    else:
+        p.seq_lens = None
+        p.seq_len = seq
+    p.batch, p.num_heads, p.head_dim = q.shape
+    p.num_kv_heads = k.shape[2]
+    p.block_size, p.num_blocks = bs, k.shape[0]
+    p.num_splits = num_splits
+    p.scale = 1.0 / math.sqrt(q.shape[2])
+    p.dtype = _native.PA_F16 if q.dtype == torch.float16 else _native.PA_BF16
+    p.out = out.data_ptr()
+    p.out_stride_b, p.out_stride_h = out.stride(0), out.stride(1)
+    p.lse = lse.data_ptr()
+    return p
+
+
+def _cases():
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(123)
+    ragged = torch.randint(0, 600, (24,), generator=g, dtype=torch.int32)
+    ragged[3] = 0
+    return [
+        ("mha_f16_uniform", workloads.build("noalloc_mha", 8, 32, 32, 16, torch.float16, 1000,
+                                            63, 8 * 63, seed=31, device="cuda"), 0),
+        ("gqa4_bf16_ragged", workloads.build("noalloc_gqa", 24, 32, 8, 16, torch.bfloat16,
+                                             ragged.cuda(), 38, 24 * 38, seed=32,
+                                             device="cuda"), 0),
+        ("gqa8_bf16_split3", workloads.build("noalloc_split", 6, 16, 2, 32, torch.bfloat16, 700,
+                                             22, 6 * 22, seed=33, device="cuda"), 3),
+    ]
+
+
+@pytest.mark.parametrize("case", range(3))
+def test_noalloc_matches_pa_decode_on_two_calls(case):
+    import paged_attention as pa
+    from paged_attention import _native
+    name, w, ns = _cases()[case]
+    # the existing entry point (caller-provided workspace)
+    ref_o, ref_lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                        w.block_size, ns or None, return_lse=True)
+    lib = _native.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    for call in range(2):
+        out = torch.full_like(w.q, float("nan"))
+        lse = torch.full((w.batch, w.num_heads), float("nan"), dtype=torch.float32,
+                         device="cuda")
+        p = _params(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len, w.block_size, out, lse,
+                    ns)
+        rc = lib.pa_decode_noalloc(ctypes.byref(p), stream)
+        assert rc == _native.PA_OK, _native.status_string(rc)
+        torch.cuda.synchronize()
+        assert_o_close(out, ref_o.float(), f"{name} call {call} O")
+        assert_lse_close(lse, ref_lse, f"{name} call {call} LSE")
+
+
+def test_noalloc_rejects_scratch_beyond_its_maximum():
+    from paged_attention import _native, workloads
+    w = workloads.build("noalloc_big", 64, 64, 64, 16, torch.float16, 512, 32, 64 * 32, seed=34,
+                        device="cuda")
+    out = torch.empty_like(w.q)
+    lse = torch.empty(w.batch, w.num_heads, dtype=torch.float32, device="cuda")
+    # split schedule, 512 splits: 64*64*512 partial rows of 516 B >> the scratch array
+    p = _params(w.q, w.k_cache, w.v_cache, w.block_table, 512, 16, out, lse, num_splits=512)
+    need = 64 * 64 * 512 * (128 + 1) * 4
+    assert need > _native.PA_NOALLOC_SCRATCH_BYTES
+    rc = _native.lib().pa_decode_noalloc(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
+    assert rc == _native.PA_ERR_WORKSPACE
