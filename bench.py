@@ -380,7 +380,7 @@ def run_b200(args, rank, world, local_rank):
     total_bytes = nbytes * world
     value = total_bytes / (eager_mean * 1e-3) / 1e9
     achieved = nbytes / (eager["mean"] * 1e-3) / 1e9
-    traffic = _profile_traffic()
+    traffic = _profile_traffic() if args.config == "c2" else None
     cpu = cpu_baseline(w, args, sample_seconds=args.cpu_seconds) if world == 1 else None
     res = {
         "metric": METRIC,

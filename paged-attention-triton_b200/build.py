@@ -21,6 +21,8 @@ INCLUDE = os.path.join(REPO, "include")
 SOURCES = [os.path.join(HERE, "csrc", "pa_decode.cu")]
 HEADERS = [os.path.join(INCLUDE, "pa_decode.h")]
 OUTPUT = os.path.join(HERE, "paged_attention", "libpa_decode.so")
+EXT_SOURCE = os.path.join(HERE, "csrc", "torch_ext.cpp")
+EXT_OUTPUT = os.path.join(HERE, "paged_attention", "_pa_ext.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -49,8 +51,49 @@ def _stale() -> bool:
     return any(os.path.getmtime(s) > out_t for s in SOURCES + HEADERS + [__file__])
 
 
+def _ext_stale() -> bool:
+    if not os.path.exists(EXT_OUTPUT):
+        return True
+    t = os.path.getmtime(EXT_OUTPUT)
+    return any(os.path.getmtime(x) > t for x in (EXT_SOURCE, HEADERS[0], OUTPUT, __file__))
+
+
+def build_extension(force: bool = False, verbose: bool = False) -> str:
+    """Compile the PyTorch binding ``paged_attention/_pa_ext.so`` (g++ against
+    torch's headers, linked to libpa_decode.so found next to it at run time)."""
+    if not force and not _ext_stale():
+        return EXT_OUTPUT
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension as ce
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_pa_ext",
+           "-DTORCH_API_INCLUDE_EXTENSION_H", f"-I{INCLUDE}", f"-I{cuda_home}/include",
+           f"-I{sysconfig.get_paths()['include']}"]
+    cmd += [f"-I{p}" for p in ce.include_paths()]
+    cmd += [EXT_SOURCE, "-o", EXT_OUTPUT + ".tmp"]
+    cmd += [f"-L{p}" for p in ce.library_paths()]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+            f"-L{os.path.dirname(OUTPUT)}", "-l:libpa_decode.so", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(EXT_OUTPUT + ".tmp", EXT_OUTPUT)
+    return EXT_OUTPUT
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if a source is newer than it; return its path."""
+    """Compile the library (and the PyTorch binding) if a source is newer."""
+    _build_library(force, verbose)
+    build_extension(force, verbose)
+    return OUTPUT
+
+
+def _build_library(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return OUTPUT
     cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", "-o", OUTPUT + ".tmp", *SOURCES]

@@ -1368,6 +1368,60 @@ static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const 
   return r == CUDA_SUCCESS;
 }
 
+// Encoded tensor maps are reused across calls: a decode loop passes the same
+// K/V cache pointers every step. Small round-robin cache, keyed by everything
+// the encoding depends on.
+struct MapKey {
+  int dev, dtype, rows, five_d;
+  const void* base;
+  int64_t dims[3];      // block_size, num_kv_heads, num_blocks
+  int64_t strides[3];   // block, slot, head (elements)
+  bool operator==(const MapKey& o) const {
+    return dev == o.dev && dtype == o.dtype && rows == o.rows && five_d == o.five_d &&
+           base == o.base && memcmp(dims, o.dims, sizeof(dims)) == 0 &&
+           memcmp(strides, o.strides, sizeof(strides)) == 0;
+  }
+};
+constexpr int kMapCache = 16;
+static MapKey g_map_keys[kMapCache];
+static CUtensorMap g_maps[kMapCache];
+static bool g_map_valid[kMapCache];
+static int g_map_next = 0;
+
+static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int dev, const void* base,
+                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows,
+                             bool five_d) {
+  MapKey key;
+  memset(&key, 0, sizeof(key));
+  key.dev = dev;
+  key.dtype = p->dtype;
+  key.rows = rows;
+  key.five_d = five_d ? 1 : 0;
+  key.base = base;
+  key.dims[0] = p->block_size;
+  key.dims[1] = p->num_kv_heads;
+  key.dims[2] = p->num_blocks;
+  key.strides[0] = s_block;
+  key.strides[1] = s_slot;
+  key.strides[2] = s_head;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 0; i < kMapCache; ++i)
+      if (g_map_valid[i] && g_map_keys[i] == key) {
+        *map = g_maps[i];
+        return true;
+      }
+  }
+  if (!encode_cache_map(map, p, base, s_block, s_slot, s_head, rows, five_d)) return false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  const int i = g_map_next;
+  g_map_next = (g_map_next + 1) % kMapCache;
+  g_map_keys[i] = key;
+  g_maps[i] = *map;
+  g_map_valid[i] = true;
+  return true;
+}
+
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 template <typename T, bool kDup, int TILE, int NW, int NS>
@@ -1535,14 +1589,14 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
 
   CUtensorMap mk, mv;
   kp.map5d = 1;
-  if (!encode_cache_map(&mk, p, p->k_cache, p->k_stride_block, p->k_stride_slot, p->k_stride_head,
-                        kp.R, true) ||
-      !encode_cache_map(&mv, p, p->v_cache, p->v_stride_block, p->v_stride_slot, p->v_stride_head,
-                        kp.R, true)) {
+  if (!cached_cache_map(&mk, p, dev, p->k_cache, p->k_stride_block, p->k_stride_slot,
+                        p->k_stride_head, kp.R, true) ||
+      !cached_cache_map(&mv, p, dev, p->v_cache, p->v_stride_block, p->v_stride_slot,
+                        p->v_stride_head, kp.R, true)) {
     kp.map5d = 0;
-    if (!encode_cache_map(&mk, p, p->k_cache, p->k_stride_block, p->k_stride_slot,
+    if (!cached_cache_map(&mk, p, dev, p->k_cache, p->k_stride_block, p->k_stride_slot,
                           p->k_stride_head, kp.R, false) ||
-        !encode_cache_map(&mv, p, p->v_cache, p->v_stride_block, p->v_stride_slot,
+        !cached_cache_map(&mv, p, dev, p->v_cache, p->v_stride_block, p->v_stride_slot,
                           p->v_stride_head, kp.R, false))
       return PA_ERR_ARG;
   }

@@ -122,6 +122,24 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+_ext = None
+
+
+def ext():
+    """The PyTorch extension module ``_pa_ext`` (next to this file; no fallback)."""
+    global _ext
+    if _ext is None:
+        lib()   # the extension links libpa_decode.so; report it first if missing
+        try:
+            from . import _pa_ext as mod
+        except ImportError as e:
+            raise NativeLibraryMissing(
+                f"paged_attention/_pa_ext is missing or broken ({e}): build it with "
+                "`python paged-attention-triton_b200/build.py` (there is no fallback)") from e
+        _ext = mod
+    return _ext
+
+
 def status_string(code: int) -> str:
     return lib().pa_status_string(code).decode()
 

@@ -7,7 +7,8 @@ shape and dtype of ``Q``; ``PagedAttentionV2Function`` keeps the reference's
 autograd wrapper whose backward raises (``torch_kernel.py:66-68``).
 
 Underneath is one launch of the sm_100a kernel through the C ABI
-(``include/pa_decode.h``), on the current CUDA stream, with no host sync, no
+(``include/pa_decode.h``), made by a thin C++ extension (``_pa_ext``, built from
+``csrc/torch_ext.cpp``) on the current CUDA stream, with no host sync, no
 Triton and no CPU fallback.
 
 Superset of the reference API (keyword-only extensions):
@@ -88,10 +89,15 @@ _workspaces: Dict[Tuple[int, int], DecodeWorkspace] = {}
 _sm_counts: Dict[int, int] = {}
 
 
+def _raw_stream(idx: int) -> int:
+    getter = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return getter(idx) if getter is not None else torch.cuda.current_stream(idx).cuda_stream
+
+
 def default_workspace(device: torch.device) -> DecodeWorkspace:
     """The workspace of the current stream on ``device`` (created on first use)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(idx).cuda_stream
+    stream = _raw_stream(idx)
     key = (idx, stream)
     ws = _workspaces.get(key)
     if ws is None:
@@ -130,111 +136,28 @@ def _decode(Q: torch.Tensor, K_Cache: torch.Tensor, V_Cache: torch.Tensor,
             return_lse: bool = False, return_partials: bool = False,
             workspace: Optional[DecodeWorkspace] = None, out: Optional[torch.Tensor] = None,
             kernel_variant: int = 0):
-    _check(Q.is_cuda and K_Cache.is_cuda and V_Cache.is_cuda and Block_Table.is_cuda,
-           "paged_attention: Q, K_Cache, V_Cache and Block_Table must be CUDA tensors")
-    _check(Q.dim() == 3, "paged_attention: Q must be [B, H, D]")
-    _check(K_Cache.dim() == 4 and V_Cache.shape == K_Cache.shape,
-           "paged_attention: K_Cache and V_Cache must both be [num_blocks, block_size, Hkv, D]")
-    _check(Q.dtype in _DTYPES, f"paged_attention: unsupported dtype {Q.dtype} (fp16 or bf16)")
-    _check(K_Cache.dtype == Q.dtype and V_Cache.dtype == Q.dtype,
-           "paged_attention: Q, K_Cache and V_Cache must share one dtype")
-    _check(Block_Table.dtype == torch.int32 and Block_Table.dim() == 2,
-           "paged_attention: Block_Table must be an int32 [B, max_blocks] tensor")
-    _check(K_Cache.device == Q.device and V_Cache.device == Q.device
-           and Block_Table.device == Q.device, "paged_attention: tensors on different devices")
-    batch, heads, dim = Q.shape
-    nblocks, bs, kv_heads, kdim = K_Cache.shape
-    _check(dim == kdim, "paged_attention: head_dim of Q and the caches differ")
-    _check(dim == HEAD_DIM, f"paged_attention: head_dim {dim} is not built (only {HEAD_DIM})")
-    _check(int(block_size) == bs, f"paged_attention: block_size {block_size} != cache block {bs}")
-    _check(bs % 8 == 0, f"paged_attention: block_size {bs} is not a multiple of 8")
-    _check(heads % kv_heads == 0, f"paged_attention: Hq={heads} is not a multiple of Hkv={kv_heads}")
-    _check(Block_Table.shape[0] == batch, "paged_attention: Block_Table rows != batch")
-    _check(Q.stride(2) == 1 and K_Cache.stride(3) == 1 and V_Cache.stride(3) == 1
-           and Block_Table.stride(1) == 1, "paged_attention: last dimensions must be contiguous")
-    if Q.stride(1) % 8 or Q.stride(0) % 8 or Q.data_ptr() % 16:
-        Q = Q.contiguous()
-    max_blocks = Block_Table.shape[1]
-
-    seq_ptr = None
-    seq_scalar = 0
-    if isinstance(seq_len, torch.Tensor):
-        _check(seq_len.numel() == batch, "paged_attention: seq_lens must have B entries")
-        if seq_len.device != Q.device or seq_len.dtype != torch.int32 or not seq_len.is_contiguous():
-            seq_len = seq_len.to(device=Q.device, dtype=torch.int32).contiguous()
-        seq_ptr = seq_len.data_ptr()
-    else:
-        seq_scalar = int(seq_len)
-        _check(0 <= seq_scalar <= max_blocks * bs,
-               f"paged_attention: seq_len {seq_scalar} exceeds Block_Table capacity {max_blocks * bs}")
-
-    if scale is None:
-        scale = 1.0 / math.sqrt(dim)
-    ns = 0 if num_splits is None else int(num_splits)
-    _check(ns >= 0, "paged_attention: num_splits must be >= 0")
-    if return_partials and ns == 0:
-        s_for_heur = seq_scalar if seq_ptr is None else max_blocks * bs
-        ns = num_splits_heuristic(batch, heads, s_for_heur, bs, device_sm_count(Q.device))
-
-    if out is None:
-        out = torch.empty((batch, heads, dim), dtype=Q.dtype, device=Q.device)
-    lse = torch.empty((batch, heads), dtype=torch.float32, device=Q.device) if return_lse else None
-    o_part = lse_part = None
-    if return_partials:
-        o_part = torch.empty((batch, heads, ns, dim), dtype=torch.float32, device=Q.device)
-        lse_part = torch.empty((batch, heads, ns), dtype=torch.float32, device=Q.device)
-
+    # Argument checks, allocation of the outputs and the launch happen in C++
+    # (paged_attention/_pa_ext, csrc/torch_ext.cpp) over the C ABI.
+    if not (Q.is_cuda and K_Cache.is_cuda and V_Cache.is_cuda and Block_Table.is_cuda):
+        raise ValueError("paged_attention: Q, K_Cache, V_Cache and Block_Table must be CUDA tensors")
     ws = workspace if workspace is not None else default_workspace(Q.device)
-    p = DecodeParams()
-    p.q = Q.data_ptr()
-    p.q_stride_b, p.q_stride_h = Q.stride(0), Q.stride(1)
-    p.k_cache = K_Cache.data_ptr()
-    p.k_stride_block, p.k_stride_slot, p.k_stride_head = K_Cache.stride(0), K_Cache.stride(1), K_Cache.stride(2)
-    p.v_cache = V_Cache.data_ptr()
-    p.v_stride_block, p.v_stride_slot, p.v_stride_head = V_Cache.stride(0), V_Cache.stride(1), V_Cache.stride(2)
-    p.block_table = Block_Table.data_ptr()
-    p.bt_stride_b = Block_Table.stride(0)
-    p.max_blocks = max_blocks
-    p.seq_lens = seq_ptr
-    p.seq_len = seq_scalar
-    p.batch, p.num_heads, p.num_kv_heads = batch, heads, kv_heads
-    p.head_dim, p.block_size, p.num_blocks = dim, bs, nblocks
-    p.num_splits = ns
-    p.scale = float(scale)
-    p.dtype = _DTYPES[Q.dtype]
-    p.out = out.data_ptr()
-    p.out_stride_b, p.out_stride_h = out.stride(0), out.stride(1)
-    p.lse = lse.data_ptr() if lse is not None else None
-    p.o_partial = o_part.data_ptr() if o_part is not None else None
-    p.lse_partial = lse_part.data_ptr() if lse_part is not None else None
-    p.kernel_variant = int(kernel_variant)
-
-    lib = _native.lib()
-    ws_bytes = ctypes.c_size_t(0)
-    n_counters = ctypes.c_size_t(0)
-    rc = lib.pa_decode_workspace(ctypes.byref(p), ctypes.byref(ws_bytes), ctypes.byref(n_counters))
-    if rc != _native.PA_OK:
-        raise PagedAttentionError("pa_decode_workspace", rc)
-    ws.ensure(ws_bytes.value, n_counters.value)
-    p.workspace = ws.buffer.data_ptr() if ws.buffer.numel() else None
-    p.workspace_bytes = ws.buffer.numel()
-    p.counters = ws.counters.data_ptr()
-    p.counter_count = ws.counters.numel()
-    p.status = ws.status.data_ptr()
-
-    stream = torch.cuda.current_stream(Q.device).cuda_stream
-    rc = lib.pa_decode(ctypes.byref(p), stream)
-    if rc != _native.PA_OK:
-        raise PagedAttentionError("pa_decode", rc)
-
-    if not (return_lse or return_partials):
-        return out
-    res = (out,)
-    if return_lse:
-        res += (lse,)
-    if return_partials:
-        res += (o_part, lse_part)
-    return res
+    if isinstance(seq_len, torch.Tensor):
+        seq_t, seq_i = seq_len, 0
+    else:
+        seq_t, seq_i = None, int(seq_len)
+    ns = 0 if num_splits is None else int(num_splits)
+    args = (Q, K_Cache, V_Cache, Block_Table, seq_t, seq_i, int(block_size), ns,
+            0.0 if scale is None else float(scale), bool(return_lse), bool(return_partials))
+    ext = _native.ext()
+    status, res, need_bytes, need_counters = ext.decode(
+        *args, ws.buffer, ws.counters, ws.status, int(kernel_variant), out)
+    if status != 0:
+        ws.ensure(need_bytes, need_counters)
+        status, res, _, _ = ext.decode(*args, ws.buffer, ws.counters, ws.status,
+                                       int(kernel_variant), out)
+        if status != 0:
+            raise PagedAttentionError("pa_decode", _native.PA_ERR_WORKSPACE)
+    return res[0] if len(res) == 1 else tuple(res)
 
 
 class PagedAttentionV2Function(torch.autograd.Function):
