@@ -38,6 +38,7 @@ namespace pa {
 constexpr int kD = 128;             // head_dim
 constexpr int kCumMax = 1024;       // rows whose tile prefix sum fits in shared memory
 constexpr int kDescInts = 12;       // per-stage tile descriptor
+constexpr int kSlotStride = 132;    // floats per merge row in shared memory (128 + LSE, 16-B aligned)
 constexpr float kSentinel = -1e30f;     // split_kv_kernel.py:8
 constexpr float kValidLse = -1e29f;     // split_kv_kernel.py:9
 constexpr float kLog2e = 1.4426950408889634f;
@@ -58,7 +59,11 @@ struct Cfg {
   static constexpr int kBarOff = kStagesBytes;
   static constexpr int kDescOff = kBarOff + NW * NS * 8;
   static constexpr int kCumOff = kDescOff + NW * NS * kDescInts * 4;
-  static constexpr int kSmem = kCumOff + (kCumMax + 1) * 4 + 1024;  // + alignment slack
+  // group merge area: NW arrival counters, then [NW][2][slot_cols][kSlotStride] floats
+  static constexpr int kGroupOff = (kCumOff + (kCumMax + 1) * 4 + 15) & ~15;
+  static constexpr int kGroupCntBytes = (NW * 4 + 15) & ~15;
+  static constexpr int kSmemBase = kGroupOff + kGroupCntBytes + 1024;  // + alignment slack
+  static constexpr int kGroupSlotBytes = NW * 2 * kSlotStride * 4;   // per slot column
 };
 
 struct KParams {
@@ -86,12 +91,8 @@ struct KParams {
   int map5d;                // 1: one 5-D copy per box covers both 64-dim halves
   int W;                    // workers
   int use_cum;              // balanced + seq_lens: prefix sums in shared memory
-  int slot_cols;            // balanced partial slot width: min(G, 8) query heads
-  int static_pct;           // balanced: share of units in static per-worker ranges (%)
-  int dyn_per_worker;       // balanced: dynamic ranges per worker (upper bound)
-  int n_seg_counters;       // arrival counters before the two schedule counters
-  int hybrid_min_units;     // balanced: dynamic ranges only above this many units per worker
-  int min_dyn_units;        // balanced: smallest dynamic range
+  int slot_cols;            // partial slot width: min(G, 8) query heads
+  int gsz;                  // warps per merge group (NW, or 1 when the slots do not fit)
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -258,14 +259,14 @@ __device__ __forceinline__ uint32_t pack16(uint16_t lo, uint16_t hi) {
 // (kv head, query chunk) pair, query chunk qc holding query heads
 // kvh*G + qc*8 .. +min(8, G - qc*8).
 //
-// Balanced schedule: units are flattened in (b, kvh, qc, tile) order and cut
-// into ranges. Range r < W (one per worker) is static, [r*Ps, min(Us, (r+1)*Ps));
-// ranges r >= W cover the remaining units in small dynamic chunks of CUd units,
-// taken in order from a global counter by whichever worker is free. A worker
-// first drains its static range, then takes dynamic ranges until none is left,
-// which absorbs per-SM bandwidth differences at the tail. A piece is the part
-// of one segment inside one range; its partial lives in slot 2r (piece starts
-// the range) or 2r+1 (piece ends the range).
+// Balanced schedule: units are flattened in (b, kvh, qc, tile) order. Group g
+// (the gsz warps of one CTA, or a single warp) owns [g*P, min(U, (g+1)*P)),
+// and warp i of the group the contiguous part [gr0 + i*Pw, ...). A piece is the
+// part of a segment inside one warp's range. Pieces of a segment inside one
+// group are merged in shared memory by the warp that finishes last; the
+// group's piece of a segment that crosses groups goes to a global partial slot
+// (2g: the piece starts the group's range, 2g+1: it ends it), and the group
+// that finishes the segment last merges those.
 //
 // Split schedule (the reference's): worker w owns split s of one segment; its
 // single range is the split's tiles, and its partial is the split's row.
@@ -293,8 +294,12 @@ __device__ __forceinline__ int find_row(const int* cum, int B, int u) {
   return lo;
 }
 
-struct Sched {        // balanced schedule, identical in every CTA
-  int U, Ps, Us, CUd, nd;
+struct Ranges {       // balanced schedule of one warp
+  int U;              // units in the step
+  int P, Pw;          // units per group range, per warp range
+  int g, gi;          // group, warp index inside the group
+  int gr0, gr1;       // group range
+  int wr0, wr1;       // warp range
 };
 
 struct Work {         // split schedule: the worker's one piece
@@ -348,29 +353,26 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const KParams& p) {
   } while (c.nt == 0);
 }
 
-__device__ __forceinline__ void range_bounds(const KParams& p, const Sched& sc, int r, int& r0,
-                                             int& r1) {
-  if (r < p.W) {
-    r0 = min(sc.U, r * sc.Ps);
-    r1 = min(sc.Us, r0 + sc.Ps);
-  } else {
-    r0 = sc.Us + (r - p.W) * sc.CUd;
-    r1 = min(sc.U, r0 + sc.CUd);
-  }
-}
+// Flags of a tile's piece (balanced).
+constexpr int kFirst = 1;      // first tile of the warp's piece
+constexpr int kLast = 2;       // last tile of the warp's piece
+constexpr int kWarpSeg = 4;    // the warp's piece is the whole segment
+constexpr int kWarpGroup = 8;  // the warp's piece is the group's whole piece
+constexpr int kGroupSeg = 16;  // the group's piece is the whole segment
 
-// Piece of the cursor's tile inside range [r0, r1) (balanced): token range,
-// flags (1 first tile of the piece, 2 last, 4 piece == whole segment), slot.
 template <int TILE>
-__device__ __forceinline__ void piece_of(const Cursor& c, int r, int r0, int r1, int& t0, int& t1,
-                                         int& flags, int& slot) {
+__device__ __forceinline__ void piece_of(const Cursor& c, const Ranges& rg, int& t0, int& t1,
+                                         int& flags) {
   const int u = c.seg_lo + c.tile;
   const int seg_hi = c.seg_lo + c.nt;
-  const int plo = max(c.seg_lo, r0), phi = min(seg_hi, r1);
+  const int plo = max(c.seg_lo, rg.wr0), phi = min(seg_hi, rg.wr1);
+  const int glo = max(c.seg_lo, rg.gr0), ghi = min(seg_hi, rg.gr1);
   t0 = (plo - c.seg_lo) * TILE;
   t1 = min(c.S, (phi - c.seg_lo) * TILE);
-  flags = (u == plo ? 1 : 0) | (u == phi - 1 ? 2 : 0) | ((plo == c.seg_lo && phi == seg_hi) ? 4 : 0);
-  slot = 2 * r + (plo == r0 ? 0 : 1);
+  flags = (u == plo ? kFirst : 0) | (u == phi - 1 ? kLast : 0) |
+          ((plo == c.seg_lo && phi == seg_hi) ? kWarpSeg : 0) |
+          ((plo == glo && phi == ghi) ? kWarpGroup : 0) |
+          ((glo == c.seg_lo && ghi == seg_hi) ? kGroupSeg : 0);
 }
 
 __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
@@ -378,13 +380,13 @@ __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
 }
 
 // Block-table page and slot of this lane's TMA box in a batch of tiles: lane L
-// serves box (L & (spt-1)) of tile (L >> lspt) of the batch [u0, u1) of range
-// r. INT_MIN: the box holds no token of its piece (not loaded; the consumer
-// masks it). One load instruction per batch and lane.
+// serves box (L & (spt-1)) of tile (L >> lspt) of the batch [u0, u1) (units of
+// the warp range, or tile ordinals of a split). INT_MIN: the box holds no token
+// of its piece (not loaded; the consumer masks it). One load per lane.
 template <int TILE>
-__device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, const Sched& sc,
-                                            const Work& w, int r, int r0, int r1, int u0, int u1,
-                                            int lane, int& phys, int& slot) {
+__device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, const Ranges& rg,
+                                            const Work& w, int u0, int u1, int lane, int& phys,
+                                            int& slot) {
   const int ord = lane >> p.lspt;
   const int j = lane & ((1 << p.lspt) - 1);
   long long off = -1;
@@ -394,8 +396,8 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
     if (p.ns == 0) {
       Cursor c;
       decode_unit<TILE>(c, p, cum, u0 + ord);
-      int fl, sl;
-      piece_of<TILE>(c, r, r0, r1, t0, t1, fl, sl);
+      int fl;
+      piece_of<TILE>(c, rg, t0, t1, fl);
       tile = c.tile;
       b = c.b;
     } else {
@@ -415,123 +417,146 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
 }
 
 // ----------------------------------------------------------------------------
-// Merge of one segment's partials (the last arriving piece runs it)
+// Merging pieces
 // ----------------------------------------------------------------------------
 // split_kv_kernel.py:101-122: skip lse <= -1e29, merge by running max, divide
-// by max(sum, 1e-20); a segment with no valid piece outputs 0 and LSE -1e30.
-// Each lane owns 4 of the 128 dims.
-struct PieceSet {     // the pieces of one segment
-  int n;              // number of pieces
-  int n_static, r_first, d_first, seg_lo;
-};
-
-__device__ __forceinline__ PieceSet pieces_of(const KParams& p, const Sched& sc, int seg_lo,
-                                              int seg_hi) {
-  PieceSet ps;
-  ps.seg_lo = seg_lo;
-  ps.n_static = 0;
-  ps.r_first = 0;
-  ps.d_first = 0;
-  if (sc.Ps > 0 && seg_lo < sc.Us) {
-    ps.r_first = seg_lo / sc.Ps;
-    ps.n_static = (min(seg_hi, sc.Us) - 1) / sc.Ps - ps.r_first + 1;
+// by max(sum, 1e-20); no valid piece gives 0 and LSE -1e30. `src(k, row, lse)`
+// locates piece k's normalised row (128 floats) and LSE; rows are read from
+// global memory through L2 (kGlobal) or from shared memory. Each lane returns
+// its 4 of the 128 dims.
+template <bool kGlobal, class Src>
+__device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, float4& out4,
+                                           float& lse_out) {
+  constexpr int kBatch = 8;   // rows in flight per lane
+  auto ld_lse = [&](int k) {
+    const float* row;
+    const float* lp;
+    src(k, row, lp);
+    return kGlobal ? __ldcg(lp) : *lp;
+  };
+  auto ld_row = [&](int k) {
+    const float* row;
+    const float* lp;
+    src(k, row, lp);
+    const float4* r4 = reinterpret_cast<const float4*>(row) + lane;
+    return kGlobal ? __ldcg(r4) : *r4;
+  };
+  const float l0 = (lane < n) ? ld_lse(lane) : kValidLse;
+  float4 v[kBatch];
+#pragma unroll
+  for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? ld_row(u) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float gmax = (l0 > kValidLse) ? l0 : kValidLse;
+  for (int k = lane + 32; k < n; k += 32) {
+    const float l = ld_lse(k);
+    if (l > kValidLse) gmax = fmaxf(gmax, l);
   }
-  int n_dyn = 0;
-  if (seg_hi > sc.Us) {
-    ps.d_first = (max(seg_lo, sc.Us) - sc.Us) / sc.CUd;
-    n_dyn = (seg_hi - 1 - sc.Us) / sc.CUd - ps.d_first + 1;
+#pragma unroll
+  for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
+  float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float gsum = 0.f;
+  for (int base = 0; base < n; base += 32) {
+    const float lb = (base == 0) ? l0 : ((base + lane < n) ? ld_lse(base + lane) : kValidLse);
+    const float wl = (lb > kValidLse) ? exp2f((lb - gmax) * kLog2e) : 0.f;
+    float ws = wl;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) ws += __shfl_xor_sync(kFull, ws, o2);
+    gsum += ws;
+    const int cnt = min(32, n - base);
+    for (int k0 = 0; k0 < cnt; k0 += kBatch) {
+      if (base + k0 > 0) {
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          v[u] = (k0 + u < cnt) ? ld_row(base + k0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float wgt = __shfl_sync(kFull, wl, (k0 + u) & 31);
+        if (k0 + u < cnt && wgt > 0.f) {
+          a4.x = fmaf(wgt, v[u].x, a4.x);
+          a4.y = fmaf(wgt, v[u].y, a4.y);
+          a4.z = fmaf(wgt, v[u].z, a4.z);
+          a4.w = fmaf(wgt, v[u].w, a4.w);
+        }
+      }
+    }
   }
-  ps.n = ps.n_static + n_dyn;
-  return ps;
+  const float inv = 1.f / fmaxf(gsum, 1e-20f);
+  out4 = make_float4(a4.x * inv, a4.y * inv, a4.z * inv, a4.w * inv);
+  lse_out = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
 }
 
 template <typename T>
-__device__ __forceinline__ void merge_segment(const KParams& p, const Sched& sc, int b, int kvh,
-                                              int qc, int gc, const PieceSet& ps, int lane) {
-  constexpr int kBatch = 8;   // partial rows in flight per lane
-  const int n = (p.ns == 0) ? ps.n : p.ns;
+__device__ __forceinline__ void store_out4(const KParams& p, int b, int hq, int lane, float4 o,
+                                           float lse) {
+  char* dst = p.out + b * p.o_sb + hq * p.o_sh + lane * 8;
+  const uint32_t lo = pack16(Mma<T>::from_float(o.x), Mma<T>::from_float(o.y));
+  const uint32_t hi = pack16(Mma<T>::from_float(o.z), Mma<T>::from_float(o.w));
+  *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+  if (lane == 0 && p.lse) p.lse[b * p.Hq + hq] = lse;
+}
+
+// Global partial slot of group g's piece: row of column j.
+__device__ __forceinline__ float* gslot_row(const KParams& p, long long slot, int j) {
+  return p.o_part + (slot * p.slot_cols + j) * kD;
+}
+__device__ __forceinline__ float* gslot_lse(const KParams& p, long long slot, int j) {
+  return p.lse_part + slot * p.slot_cols + j;
+}
+
+// The last group to finish a segment merges the groups' partials.
+template <typename T>
+__device__ __forceinline__ void merge_groups(const KParams& p, const Ranges& rg, int b, int kvh,
+                                             int qc, int gc, int seg_lo, int seg_hi, int lane) {
+  const int g_first = seg_lo / rg.P;
+  const int n = (seg_hi - 1) / rg.P - g_first + 1;
+  for (int j = 0; j < gc; ++j) {
+    auto src = [&](int k, const float*& row, const float*& lp) {
+      const int g = g_first + k;
+      const long long sl = 2ll * g + (max(seg_lo, g * rg.P) == g * rg.P ? 0 : 1);
+      row = gslot_row(p, sl, j);
+      lp = gslot_lse(p, sl, j);
+    };
+    float4 o4;
+    float lse;
+    merge_rows<true>(n, lane, src, o4, lse);
+    store_out4<T>(p, b, kvh * p.G + qc * 8 + j, lane, o4, lse);
+  }
+}
+
+// Split schedule: the last split of a segment merges rows [b, hq, 0..ns).
+template <typename T>
+__device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, int qc, int gc,
+                                             int lane) {
   for (int j = 0; j < gc; ++j) {
     const int hq = kvh * p.G + qc * 8 + j;
-    auto part = [&](int k, const float*& op, const float*& lp) {
-      if (p.ns == 0) {
-        int r, r_start;
-        if (k < ps.n_static) {
-          r = ps.r_first + k;
-          r_start = r * sc.Ps;
-        } else {
-          const int d = ps.d_first + (k - ps.n_static);
-          r = p.W + d;
-          r_start = sc.Us + d * sc.CUd;
-        }
-        const long long sl = 2ll * r + (max(ps.seg_lo, r_start) == r_start ? 0 : 1);
-        op = p.o_part + (sl * p.slot_cols + j) * kD;
-        lp = p.lse_part + sl * p.slot_cols + j;
-      } else {
-        const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + k;
-        op = p.o_part + row * kD;
-        lp = p.lse_part + row;
-      }
+    const long long row0 = (static_cast<long long>(b) * p.Hq + hq) * p.ns;
+    auto src = [&](int k, const float*& row, const float*& lp) {
+      row = p.o_part + (row0 + k) * kD;
+      lp = p.lse_part + row0 + k;
     };
-    auto row4 = [&](int k) {
-      const float* op;
-      const float* lp;
-      part(k, op, lp);
-      return __ldcg(reinterpret_cast<const float4*>(op) + lane);
-    };
-    auto lse_of = [&](int k) {
-      const float* op;
-      const float* lp;
-      part(k, op, lp);
-      return __ldcg(lp);
-    };
-    // One round trip for the common case: the LSEs of the first 32 pieces
-    // (one per lane) and the rows of the first kBatch pieces are in flight together.
-    const float l0 = (lane < n) ? lse_of(lane) : kValidLse;
-    float4 v[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? row4(u) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float gmax = (l0 > kValidLse) ? l0 : kValidLse;
-    for (int k = lane + 32; k < n; k += 32) {
-      const float l = lse_of(k);
-      if (l > kValidLse) gmax = fmaxf(gmax, l);
-    }
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
-    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float gsum = 0.f;
-    for (int base = 0; base < n; base += 32) {
-      const float lb = (base == 0) ? l0 : ((base + lane < n) ? lse_of(base + lane) : kValidLse);
-      const float wl = (lb > kValidLse) ? exp2f((lb - gmax) * kLog2e) : 0.f;
-      float ws = wl;
-#pragma unroll
-      for (int o2 = 16; o2 > 0; o2 >>= 1) ws += __shfl_xor_sync(kFull, ws, o2);
-      gsum += ws;
-      const int cnt = min(32, n - base);
-      for (int k0 = 0; k0 < cnt; k0 += kBatch) {
-        if (base + k0 > 0) {
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u)
-            v[u] = (k0 + u < cnt) ? row4(base + k0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const float wgt = __shfl_sync(kFull, wl, (k0 + u) & 31);
-          if (k0 + u < cnt && wgt > 0.f) {
-            a4.x = fmaf(wgt, v[u].x, a4.x);
-            a4.y = fmaf(wgt, v[u].y, a4.y);
-            a4.z = fmaf(wgt, v[u].z, a4.z);
-            a4.w = fmaf(wgt, v[u].w, a4.w);
-          }
-        }
-      }
-    }
-    const float inv = 1.f / fmaxf(gsum, 1e-20f);
-    char* dst = p.out + b * p.o_sb + hq * p.o_sh + lane * 8;
-    const uint32_t lo = pack16(Mma<T>::from_float(a4.x * inv), Mma<T>::from_float(a4.y * inv));
-    const uint32_t hi = pack16(Mma<T>::from_float(a4.z * inv), Mma<T>::from_float(a4.w * inv));
-    *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-    if (lane == 0 && p.lse) p.lse[b * p.Hq + hq] = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
+    float4 o4;
+    float lse;
+    merge_rows<true>(p.ns, lane, src, o4, lse);
+    store_out4<T>(p, b, hq, lane, o4, lse);
   }
+}
+
+// Publishes the group's piece (already written to its global slot) and merges
+// the segment if this group arrived last.
+template <typename T>
+__device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg, int b, int kvh,
+                                              int qc, int gc, int seg_lo, int seg_hi, int lane) {
+  __threadfence();
+  __syncwarp();
+  const int n = (seg_hi - 1) / rg.P - seg_lo / rg.P + 1;
+  const int cid = (b * p.Hkv + kvh) * p.QC + qc;
+  int last = 0;
+  if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == n - 1);
+  last = __shfl_sync(kFull, last, 0);
+  if (!last) return;
+  __threadfence();
+  merge_groups<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+  if (lane == 0) atomicExch(p.counters + cid, 0);
 }
 
 // ----------------------------------------------------------------------------
@@ -549,6 +574,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   int* descs = reinterpret_cast<int*>(smem + C::kDescOff);
   int* cum = reinterpret_cast<int*>(smem + C::kCumOff);
+  int* gcnt = reinterpret_cast<int*>(smem + C::kGroupOff);         // [NW] arrival counters
+  float* gslots = reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
   __shared__ int warp_tot[NW];
 
   const int warp = threadIdx.x >> 5;
@@ -562,6 +589,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&bars[warp * NS + s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (threadIdx.x < NW) gcnt[threadIdx.x] = 0;
 
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
   if (p.ns == 0 && p.use_cum) {
@@ -612,51 +640,27 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
 
   // ---------------------------------------------------------------- schedule
-  const int wid = warp * gridDim.x + blockIdx.x;
+  const int wid = blockIdx.x * NW + warp;
   const int G = p.G;
   const int spt_mask = (1 << p.lspt) - 1;
   const int bt_tiles = 32 >> p.lspt;          // tiles per page batch (one box per lane)
-  int* sched_ctr = p.counters + p.n_seg_counters;   // [0] next dynamic range, [1] workers done
-  Sched sc;
-  sc.U = sc.Ps = sc.Us = sc.nd = 0;
-  sc.CUd = 1;
+  Ranges rg;
+  rg.U = rg.P = rg.Pw = rg.g = rg.gi = rg.gr0 = rg.gr1 = rg.wr0 = rg.wr1 = 0;
   Work w;
   w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
-  int rc = -1, r0c = 0, r1c = 0, u0c = 0, u1c = 0;   // current page batch: range, units
-  int pend = 0;                                       // lane 0: prefetched dynamic range id
+  int n_tiles = 0;
   if (p.ns == 0) {
-    const int W = p.W;
-    sc.U = p.use_cum ? cum[p.B] : p.B * p.Hkv * p.QC * ((p.seq_len + TILE - 1) / TILE);
-    if (static_cast<long long>(sc.U) <= static_cast<long long>(p.hybrid_min_units) * W) {
-      // small step: static ranges only (dynamic ranges would cost more than the tail)
-      sc.Ps = max(1, (sc.U + W - 1) / W);
-      sc.Us = sc.U;
-    } else {
-      sc.Ps = static_cast<int>(static_cast<long long>(sc.U) * p.static_pct / (100ll * W));
-      sc.Us = sc.Ps * W;
-      const int ud = sc.U - sc.Us;
-      const int want = p.dyn_per_worker * W;
-      sc.CUd = max(p.min_dyn_units, (ud + want - 1) / want);
-      sc.nd = (ud + sc.CUd - 1) / sc.CUd;
-    }
-    rc = wid;
-    range_bounds(p, sc, rc, r0c, r1c);
-    if (r0c >= r1c) {
-      rc = -1;
-      if (sc.nd > 0) {
-        if (lane == 0) pend = W + atomicAdd(sched_ctr, 1);
-        const int nr = __shfl_sync(kFull, pend, 0);
-        if (nr < W + sc.nd) {
-          rc = nr;
-          range_bounds(p, sc, rc, r0c, r1c);
-        }
-      }
-    }
-    u0c = r0c;
-    u1c = min(r1c, r0c + bt_tiles);
-    // The id of the next dynamic range is requested one page batch before it is
-    // needed: when the batch being prepared is the last of its range.
-    if (rc >= 0 && sc.nd > 0 && u1c >= r1c && lane == 0) pend = W + atomicAdd(sched_ctr, 1);
+    rg.U = p.use_cum ? cum[p.B] : p.B * p.Hkv * p.QC * ((p.seq_len + TILE - 1) / TILE);
+    const int ngroups = gridDim.x * NW / p.gsz;
+    rg.P = max((rg.U + ngroups - 1) / ngroups, p.gsz);
+    rg.Pw = (rg.P + p.gsz - 1) / p.gsz;
+    rg.g = wid / p.gsz;
+    rg.gi = wid - rg.g * p.gsz;
+    rg.gr0 = min(rg.U, rg.g * rg.P);
+    rg.gr1 = min(rg.U, rg.gr0 + rg.P);
+    rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
+    rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
+    n_tiles = rg.wr1 - rg.wr0;
   } else {
     const int total = p.B * p.Hkv * p.QC * p.ns;
     if (wid >= total) return;
@@ -674,33 +678,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
     w.t1 = min(w.t0 + ss, S);
     w.tl0 = w.t0 / TILE;
     w.n = (w.t0 < w.t1) ? ((w.t1 - 1) / TILE - w.tl0 + 1) : 0;
-    if (w.n > 0) {
-      rc = w.s;
-      r0c = 0;
-      r1c = w.n;
-      u0c = 0;
-      u1c = min(w.n, bt_tiles);
-    }
+    n_tiles = w.n;
   }
-
-  // Successor of a page batch: the rest of its range, else the next dynamic range.
-  auto succ = [&](int& r, int& r0, int& r1, int& u0, int& u1) {
-    if (r < 0) return;
-    if (u1 < r1) {
-      u0 = u1;
-      u1 = min(r1, u0 + bt_tiles);
-    } else {
-      r = -1;
-      if (p.ns != 0 || sc.nd == 0) return;
-      const int nr = __shfl_sync(kFull, pend, 0);
-      if (nr >= p.W + sc.nd) return;
-      r = nr;
-      range_bounds(p, sc, r, r0, r1);
-      u0 = r0;
-      u1 = min(r1, r0 + bt_tiles);
-    }
-    if (p.ns == 0 && sc.nd > 0 && u1 >= r1 && lane == 0) pend = p.W + atomicAdd(sched_ctr, 1);
-  };
+  // range of this warp's units (balanced) or of its split's tile ordinals
+  const int range0 = (p.ns == 0) ? rg.wr0 : 0;
+  const int range1 = (p.ns == 0) ? rg.wr1 : w.n;
 
   const uint32_t stage0 = smem_u32(smem + warp * NS * C::kStage);
   const uint32_t bar0 = smem_u32(&bars[warp * NS]);
@@ -708,7 +690,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
   // Split schedule, empty split (split_kv_kernel.py:32-33): the partial LSE keeps
   // the sentinel; the last arriving split of the segment merges.
-  bool merge_empty = false;
   if (p.ns != 0 && w.n == 0) {
     const int gc = min(8, G - w.qc * 8);
     for (int j = 0; j < gc; ++j) {
@@ -725,35 +706,36 @@ __global__ void __launch_bounds__(NW * 32, 1)
     last = __shfl_sync(kFull, last, 0);
     if (!last) return;
     __threadfence();
-    merge_empty = true;
+    merge_splits<T>(p, w.b, w.kvh, w.qc, gc, lane);
+    if (lane == 0) atomicExch(p.counters + cid, 0);
+    return;
   }
 
-  // ---- issuer: current batch (pages pg_c/sl_c), next batch (pg_n/sl_n), cursor
+  // ---- issuer: page batches of <= 32 boxes, current (pg_c) and next (pg_n)
+  int u0c = range0, u1c = min(range1, range0 + bt_tiles);
+  int u0n = u1c, u1n = min(range1, u1c + bt_tiles);
   int pg_c = INT_MIN, sl_c = 0, pg_n = INT_MIN, sl_n = 0;
-  int rn = rc, r0n = r0c, r1n = r1c, u0n = u0c, u1n = u1c;
-  if (rc >= 0) batch_pages<TILE>(p, cum, sc, w, rc, r0c, r1c, u0c, u1c, lane, pg_c, sl_c);
-  succ(rn, r0n, r1n, u0n, u1n);
-  if (rn >= 0) batch_pages<TILE>(p, cum, sc, w, rn, r0n, r1n, u0n, u1n, lane, pg_n, sl_n);
+  if (u0c < u1c) batch_pages<TILE>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
+  if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   Cursor ic;
   ic.b = w.b;
   ic.kvh = w.kvh;
   ic.qc = w.qc;
   ic.tile = w.tl0;
   ic.nt = ic.S = ic.seg_lo = 0;
-  if (rc >= 0 && p.ns == 0) decode_unit<TILE>(ic, p, cum, u0c);
+  if (p.ns == 0 && n_tiles > 0) decode_unit<TILE>(ic, p, cum, range0);
   int ord = 0;          // tile ordinal within the current batch
   int issued = 0;
 
   auto issue = [&](int st) {
-    int t0, t1, fl, slot;
+    int t0, t1, fl;
     if (p.ns == 0) {
-      piece_of<TILE>(ic, rc, r0c, r1c, t0, t1, fl, slot);
+      piece_of<TILE>(ic, rg, t0, t1, fl);
     } else {
       const int k = u0c + ord;
       t0 = w.t0;
       t1 = w.t1;
-      fl = (k == 0 ? 1 : 0) | (k == w.n - 1 ? 2 : 0);
-      slot = w.s;
+      fl = (k == 0 ? kFirst : 0) | (k == w.n - 1 ? kLast : 0);
     }
     const int gc = min(8, G - ic.qc * 8);
     const int src = (ord << p.lspt) + (lane & spt_mask);
@@ -767,12 +749,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
     const unsigned vm = __ballot_sync(kFull, valid);
     const uint32_t bar = bar0 + st * 8;
     const uint32_t sk = stage0 + st * C::kStage;
-    const bool first = fl & 1;
+    const bool first = fl & kFirst;
     if (lane == 0) {
       int* d = desc0 + st * kDescInts;
       reinterpret_cast<int4*>(d)[0] = make_int4(ic.b, ic.kvh, ic.qc, ic.tile * TILE);
       reinterpret_cast<int4*>(d)[1] = make_int4(t0, t1, ic.seg_lo, ic.seg_lo + ic.nt);
-      reinterpret_cast<int4*>(d)[2] = make_int4(fl, gc, slot, 0);
+      reinterpret_cast<int4*>(d)[2] = make_int4(fl, gc, 0, 0);
       mbar_expect_tx(bar, __popc(vm) * 4 * p.R * 128 + (first ? gc * kD * 2 : 0));
     }
     __syncwarp();
@@ -795,28 +777,19 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     ++issued;
     // advance to the next tile
-    if (u0c + ++ord < u1c) {
-      if (p.ns == 0) cursor_next<TILE>(ic, p); else ++ic.tile;
-      return;
-    }
-    const bool same_range = (rn == rc);
-    rc = rn;
-    r0c = r0n;
-    r1c = r1n;
+    if (p.ns == 0) cursor_next<TILE>(ic, p); else ++ic.tile;
+    if (u0c + ++ord < u1c) return;
     u0c = u0n;
     u1c = u1n;
     pg_c = pg_n;
     sl_c = sl_n;
     ord = 0;
-    if (rc < 0) return;
-    succ(rn, r0n, r1n, u0n, u1n);
-    if (rn >= 0) batch_pages<TILE>(p, cum, sc, w, rn, r0n, r1n, u0n, u1n, lane, pg_n, sl_n);
-    if (p.ns != 0) ++ic.tile;
-    else if (same_range) cursor_next<TILE>(ic, p);
-    else decode_unit<TILE>(ic, p, cum, u0c);
+    u0n = u1c;
+    u1n = min(range1, u1c + bt_tiles);
+    if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   };
 
-  for (int s = 0; s < NS && rc >= 0; ++s) issue(s);
+  for (int s = 0; s < NS && issued < n_tiles; ++s) issue(s);
 
   // ---- consumer state
   uint32_t qf[8][2];
@@ -850,9 +823,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
   }
 
-  bool aborted = false;
   int st = 0;
-  for (int i = 0; i < issued; ++i) {
+  for (int i = 0; i < n_tiles; ++i) {
     const uint32_t sk = stage0 + st * C::kStage;
     const uint32_t sv = sk + C::kKV;
     const uint32_t sq = sk + 2 * C::kKV;
@@ -864,8 +836,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
         const int s2 = (st + k) % NS;
         mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1);
       }
-      aborted = true;
-      break;
+      return;
     }
     phase ^= 1u << st;
     const int* d = desc0 + st * kDescInts;
@@ -874,7 +845,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     const int4 d2 = reinterpret_cast<const int4*>(d)[2];
     const int tb = d0.w, t0 = d1.x, t1 = d1.y, fl = d2.x, gc = d2.y;
 
-    if (fl & 1) {
+    if (fl & kFirst) {
       // Query fragments (B operand of S^T = K Q^T): column n -> query head.
       const int n = rr;
       const int head = kDup ? (n < 2 * gc ? (n < gc ? n : n - gc) : -1) : (n < gc ? n : -1);
@@ -1013,13 +984,13 @@ __global__ void __launch_bounds__(NW * 32, 1)
     __syncwarp();
     const int cur = st;
     st = (st + 1 == NS) ? 0 : st + 1;
-    if (rc >= 0) issue(cur);
+    if (issued < n_tiles) issue(cur);
 
-    if (!(fl & 2)) continue;
+    if (!(fl & kLast)) continue;
 
     // ---------------------------------------------------------- piece epilogue
     const int b = d0.x, kvh = d0.y, qc = d0.z;
-    const int seg_lo = d1.z, seg_hi = d1.w, slot = d2.z;
+    const int seg_lo = d1.z, seg_hi = d1.w;
     float lsum[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -1044,7 +1015,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
         o[md][r] = v;
       }
 
-    const bool final_out = (p.ns == 0) && (fl & 4);
+    // Where this warp's piece goes: 0 final output, 1 the group's global slot
+    // (or the split's row), 2 this warp's shared-memory slot.
+    const int dest = (p.ns != 0) ? 1 : (fl & kWarpSeg) ? 0 : (fl & kWarpGroup) ? 1 : 2;
+    const int glo = max(seg_lo, rg.gr0), ghi = min(seg_hi, rg.gr1);
+    const long long gslot = 2ll * rg.g + (glo == rg.gr0 ? 0 : 1);
+    const int wside = (max(seg_lo, rg.wr0) == rg.wr0) ? 0 : 1;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = qd * 2 + e;
@@ -1053,7 +1029,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       const float lv = fmaxf(lsum[e], 1e-20f);
       const float inv_l = 1.f / lv;
       const float lse = (m_run[e] * scl + log2f(lv)) * kLn2;
-      if (final_out) {
+      if (dest == 0) {
         char* dst = p.out + b * p.o_sb + hq * p.o_sh;
 #pragma unroll
         for (int md = 0; md < 8; ++md) {
@@ -1066,11 +1042,14 @@ __global__ void __launch_bounds__(NW * 32, 1)
       } else {
         float* od;
         float* ld;
-        if (p.ns == 0) {
-          od = p.o_part + (static_cast<long long>(slot) * p.slot_cols + c) * kD;
-          ld = p.lse_part + static_cast<long long>(slot) * p.slot_cols + c;
+        if (dest == 2) {
+          od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * kSlotStride;
+          ld = od + kD;
+        } else if (p.ns == 0) {
+          od = gslot_row(p, gslot, c);
+          ld = gslot_lse(p, gslot, c);
         } else {
-          const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + slot;
+          const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + w.s;
           od = p.o_part + row * kD;
           ld = p.lse_part + row;
         }
@@ -1083,39 +1062,58 @@ __global__ void __launch_bounds__(NW * 32, 1)
         if (rr == 0) *ld = lse;
       }
     }
-    if (final_out) continue;
+    if (dest == 0) continue;
 
-    // Publish the partial; the last arriving piece merges the segment.
-    __threadfence();
+    if (p.ns != 0) {
+      // split schedule: the last split of the segment merges all ns rows
+      __threadfence();
+      __syncwarp();
+      const int cid = (b * p.Hkv + kvh) * p.QC + qc;
+      int last = 0;
+      if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == p.ns - 1);
+      last = __shfl_sync(kFull, last, 0);
+      if (!last) continue;
+      __threadfence();
+      merge_splits<T>(p, b, kvh, qc, gc, lane);
+      if (lane == 0) atomicExch(p.counters + cid, 0);
+      continue;
+    }
+    if (dest == 1) {
+      publish_group<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+      continue;
+    }
+
+    // Shared-memory piece: the group's last warp on this piece merges the
+    // warps' rows into the group's piece.
+    __threadfence_block();
     __syncwarp();
-    PieceSet ps;
-    ps.n = 0;
-    if (p.ns == 0) ps = pieces_of(p, sc, seg_lo, seg_hi);
-    const int n_expect = (p.ns == 0) ? ps.n : p.ns;
-    const int cid = (b * p.Hkv + kvh) * p.QC + qc;
+    const int w_first = (glo - rg.gr0) / rg.Pw;
+    const int nw = (ghi - 1 - rg.gr0) / rg.Pw - w_first + 1;
     int last = 0;
-    if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == n_expect - 1);
+    if (lane == 0) last = (atomicAdd(gcnt + w_first, 1) == nw - 1);
     last = __shfl_sync(kFull, last, 0);
     if (!last) continue;
-    __threadfence();
-    merge_segment<T>(p, sc, b, kvh, qc, gc, ps, lane);
-    if (lane == 0) atomicExch(p.counters + cid, 0);
-  }
-
-  if (merge_empty) {
-    const int gc = min(8, G - w.qc * 8);
-    PieceSet ps;
-    ps.n = 0;
-    merge_segment<T>(p, sc, w.b, w.kvh, w.qc, gc, ps, lane);
-    if (lane == 0) atomicExch(p.counters + (w.b * p.Hkv + w.kvh) * p.QC + w.qc, 0);
-  }
-
-  // Dynamic ranges: the last worker to finish rewinds the range counter.
-  if (p.ns == 0 && sc.nd > 0 && !aborted && lane == 0) {
-    if (atomicAdd(sched_ctr + 1, 1) == p.W - 1) {
-      atomicExch(sched_ctr, 0);
-      atomicExch(sched_ctr + 1, 0);
+    __threadfence_block();
+    if (lane == 0) gcnt[w_first] = 0;
+    for (int j = 0; j < gc; ++j) {
+      auto src = [&](int k, const float*& row, const float*& lp) {
+        const int wk = w_first + k;
+        const int start = rg.gr0 + wk * rg.Pw;
+        const int side = (max(glo, start) == start) ? 0 : 1;
+        row = gslots + ((wk * 2 + side) * p.slot_cols + j) * kSlotStride;
+        lp = row + kD;
+      };
+      float4 o4;
+      float lse;
+      merge_rows<false>(nw, lane, src, o4, lse);
+      if (fl & kGroupSeg) {
+        store_out4<T>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
+      } else {
+        *(reinterpret_cast<float4*>(gslot_row(p, gslot, j)) + lane) = o4;
+        if (lane == 0) *gslot_lse(p, gslot, j) = lse;
+      }
     }
+    if (!(fl & kGroupSeg)) publish_group<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
   }
 }
 
@@ -1228,10 +1226,9 @@ static const Variant kVariants[] = {
     {16, 8, 2},   // 5
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
-constexpr int kStaticPct = 80;      // balanced: units in static per-worker ranges
-constexpr int kDynPerWorker = 3;    // balanced: dynamic ranges per worker (bound)
-constexpr int kHybridMinUnits = 1 << 20;  // balanced: static only up to this many units per worker
-constexpr int kMinDynUnits = 4;     // balanced: smallest dynamic range
+// Opt-in shared memory per CTA is 227 KB (232448 B), static plus dynamic; the
+// kernel's static shared memory (a few words) gets a 1 KB margin.
+constexpr int kMaxSmem = 232448 - 1024;
 
 struct Plan {
   int ns = 0;        // 0: balanced
@@ -1242,16 +1239,26 @@ struct Plan {
   int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
   int slot_cols = 1;
-  bool dyn_slots = false;  // balanced: room for dynamic-range partials
+  int gsz = 1;             // balanced: warps per merge group
+  int smem = 0;            // dynamic shared memory of the launch
   size_t ws_bytes = 0;
-  size_t seg_counters = 0;
   size_t counters = 0;
 };
 
-// Partial slots of the balanced schedule: two per static range, plus two per
-// dynamic range when the hybrid schedule can occur.
-static size_t plan_slots(const Plan& pl) {
-  return static_cast<size_t>(2) * pl.W * (1 + (pl.dyn_slots ? kDynPerWorker : 0));
+// Shared memory a variant needs before the group merge area.
+template <bool kDup, int TILE, int NW, int NS>
+static int smem_base() {
+  return Cfg<kDup, TILE, NW, NS>::kSmemBase;
+}
+
+static int variant_smem_base(int variant, bool dup) {
+  switch (variant) {
+    case 2: return dup ? smem_base<true, 16, 8, 3>() : 0;
+    case 3: return dup ? smem_base<true, 32, 6, 2>() : smem_base<false, 32, 6, 2>();
+    case 4: return dup ? smem_base<true, 16, 12, 2>() : 0;
+    case 5: return dup ? smem_base<true, 16, 8, 2>() : smem_base<false, 16, 8, 2>();
+    default: return dup ? smem_base<true, 32, 4, 3>() : smem_base<false, 32, 4, 3>();
+  }
 }
 
 static pa_status_t validate(const pa_decode_params* p) {
@@ -1273,13 +1280,16 @@ static pa_status_t validate(const pa_decode_params* p) {
   return PA_OK;
 }
 
-// Automatic choice, from B200 sweeps of the five benchmark shapes: pages
-// shorter than 32 tokens stream best as 16-token tiles on 8 warps (one page per
-// box, two boxes per K/V tile would double the copies); longer pages as
+// Automatic choice, from B200 sweeps of the five benchmark shapes: MHA with
+// pages shorter than 32 tokens, and groups larger than 4 query heads, stream
+// best as 16-token tiles on 8 warps; longer pages and 2- or 4-head groups as
 // 32-token tiles on 6 warps.
 static int pick_variant(const pa_decode_params* p, bool dup) {
   int v = p->kernel_variant;
-  if (v == 0) v = (p->block_size < 32) ? 5 : 3;
+  if (v == 0) {
+    const int g = p->num_heads / p->num_kv_heads;
+    v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
+  }
   if (!dup && (v == 2 || v == 4)) v = 5;
   return v;
 }
@@ -1308,13 +1318,15 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     pl.grid = sms;
     pl.W = pl.grid * v.nw;
     pl.use_cum = p->seq_lens != nullptr;
-    // Dynamic ranges exist only when a step can exceed kHybridMinUnits units
-    // per worker; otherwise only the 2W static slots are ever written.
-    const long long u_max = static_cast<long long>(p->batch) * nseg *
-                            ((cap + v.tile - 1) / v.tile);
-    pl.dyn_slots = u_max > static_cast<long long>(kHybridMinUnits) * pl.W;
-    pl.ws_bytes = plan_slots(pl) * pl.slot_cols * (kD + 1) * sizeof(float);
+    // Merge pieces inside a CTA through shared memory when the warps' rows fit.
+    const int base = variant_smem_base(pl.variant, pl.dup);
+    const int group_bytes = v.nw * 2 * kSlotStride * 4 * pl.slot_cols;
+    pl.gsz = (base + group_bytes <= kMaxSmem) ? v.nw : 1;
+    pl.smem = base + (pl.gsz > 1 ? group_bytes : 0);
+    const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);   // two per group
+    pl.ws_bytes = slots * pl.slot_cols * (kD + 1) * sizeof(float);
   } else {
+    pl.smem = variant_smem_base(pl.variant, pl.dup);
     const long long workers = static_cast<long long>(p->batch) * nseg * pl.ns;
     if (workers > 0x7fffffffll) return PA_ERR_UNSUPPORTED;
     pl.W = static_cast<int>(workers);
@@ -1322,8 +1334,7 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
     pl.ws_bytes = (p->o_partial && p->lse_partial) ? 0 : rows * (kD + 1) * sizeof(float);
   }
-  pl.seg_counters = static_cast<size_t>(p->batch) * nseg;
-  pl.counters = pl.seg_counters + 2;   // + dynamic-range counter and done counter
+  pl.counters = static_cast<size_t>(p->batch) * nseg;
   return PA_OK;
 }
 
@@ -1428,19 +1439,19 @@ template <typename T, bool kDup, int TILE, int NW, int NS>
 static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                               const KParams& kp, cudaStream_t stream, int dev) {
   using C = Cfg<kDup, TILE, NW, NS>;
-  static_assert(C::kSmem <= 232448, "shared memory plan exceeds 227 KB");
+  static_assert(C::kSmemBase <= kMaxSmem, "shared memory plan exceeds 227 KB");
   static bool attr_set[64] = {false};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!attr_set[dev]) {
       const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 C::kSmem);
+                                                 kMaxSmem);
       if (e != cudaSuccess) return e;
       attr_set[dev] = true;
     }
   }
-  pa_decode_kernel<T, kDup, TILE, NW, NS><<<pl.grid, NW * 32, C::kSmem, stream>>>(mk, mv, kp);
+  pa_decode_kernel<T, kDup, TILE, NW, NS><<<pl.grid, NW * 32, pl.smem, stream>>>(mk, mv, kp);
   return cudaGetLastError();
 }
 
@@ -1557,7 +1568,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   if (pl.ns == 0) {
     float* ws = static_cast<float*>(p->workspace);
     kp.o_part = ws;
-    kp.lse_part = ws + plan_slots(pl) * pl.slot_cols * kD;
+    kp.lse_part = ws + static_cast<size_t>(2) * (pl.W / pl.gsz) * pl.slot_cols * kD;
   } else if (p->o_partial && p->lse_partial) {
     kp.o_part = p->o_partial;
     kp.lse_part = p->lse_partial;
@@ -1581,11 +1592,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.W = pl.W;
   kp.use_cum = pl.use_cum ? 1 : 0;
   kp.slot_cols = pl.slot_cols;
-  kp.static_pct = kStaticPct;
-  kp.dyn_per_worker = kDynPerWorker;
-  kp.n_seg_counters = static_cast<int>(pl.seg_counters);
-  kp.hybrid_min_units = pl.dyn_slots ? kHybridMinUnits : INT_MAX;
-  kp.min_dyn_units = kMinDynUnits;
+  kp.gsz = pl.gsz;
 
   CUtensorMap mk, mv;
   kp.map5d = 1;
