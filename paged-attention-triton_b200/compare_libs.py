@@ -1,0 +1,179 @@
+"""Same-GPU comparison with library paged-attention decode kernels.
+
+    python compare_libs.py [--configs c1,c2,c3,c4,c5] [--iters 50]
+
+For each benchmark shape it times this operator, vLLM's
+``paged_attention_v1`` / ``paged_attention_v2`` (the kernels the reference's
+Layer-4 benchmark calls, ``tests/benchmark_vllm.py:9-89``) and FlashInfer's
+``BatchDecodeWithPagedKVCacheWrapper``, all on the same inputs, and checks that
+their outputs agree with this operator's within the parity tolerance. The
+reference passes v2's arguments as ``(out, tmp_out, exp_sums, max_logits, ...)``
+(``tests/benchmark_vllm.py:58``); vLLM's signature is
+``(out, exp_sum, max_logits, tmp_out, ...)``, which is what is used here.
+
+vLLM stores K as ``[blocks, Hkv, D/x, block, x]`` and V as ``[blocks, Hkv, D,
+block]``; the caches are re-laid out once, outside the timed region. FlashInfer
+reads the ``[blocks, block, Hkv, D]`` (NHD) layout this operator uses.
+Timing: L2 flushed before every call (512 MB write, then 512 MB read), CUDA
+events around the call only, median of ``--iters`` calls.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+import paged_attention as pa  # noqa: E402
+from paged_attention import workloads  # noqa: E402
+
+
+class _Flush:
+    def __init__(self):
+        self.w = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+        self.r = torch.ones(128 << 20, dtype=torch.int32, device="cuda")
+
+    def __call__(self):
+        self.w.fill_(1)
+        self.r.sum(dtype=torch.int64)
+
+
+def _time(fn, flush, iters):
+    fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e) * 1e3)
+    times.sort()
+    return times[len(times) // 2]
+
+
+def _close(a, b):
+    a = a.float()
+    b = b.float()
+    return bool(((a - b).abs() <= 2e-3 + 1e-2 * b.abs()).all())
+
+
+def _vllm_runners(w, lens, max_s, scale):
+    try:
+        from vllm import _custom_ops as ops
+    except Exception as e:  # vLLM missing or not built for this GPU
+        return {}, f"vllm unavailable: {type(e).__name__}"
+    q, k, v = w.q, w.k_cache, w.v_cache
+    nb, bs, hkv, d = k.shape
+    x = 16 // k.element_size()
+    kv = k.view(nb, bs, hkv, d // x, x).permute(0, 2, 3, 1, 4).contiguous()
+    vv = v.permute(0, 2, 3, 1).contiguous()
+    out = torch.empty_like(q)
+    one = torch.tensor(1.0, dtype=torch.float32, device="cuda")
+    runners = {}
+
+    def v1():
+        ops.paged_attention_v1(out, q, kv, vv, hkv, scale, w.block_table, lens, bs, max_s, None,
+                               "auto", one, one)
+        return out
+
+    if max_s <= 8192:
+        runners["vllm_v1"] = v1
+    parts = (max_s + 511) // 512
+    exp_sum = torch.empty(q.shape[0], q.shape[1], parts, dtype=torch.float32, device="cuda")
+    max_logits = torch.empty_like(exp_sum)
+    tmp = torch.empty(q.shape[0], q.shape[1], parts, d, dtype=q.dtype, device="cuda")
+
+    def v2():
+        ops.paged_attention_v2(out, exp_sum, max_logits, tmp, q, kv, vv, hkv, scale,
+                               w.block_table, lens, bs, max_s, None, "auto", one, one)
+        return out
+
+    runners["vllm_v2"] = v2
+    return runners, None
+
+
+def _flashinfer_runner(w, lens_list, scale):
+    try:
+        import flashinfer
+    except Exception as e:
+        return None, f"flashinfer unavailable: {type(e).__name__}"
+    q, k, v = w.q, w.k_cache, w.v_cache
+    bs = w.block_size
+    npages = [(s + bs - 1) // bs for s in lens_list]
+    indptr = [0]
+    for n in npages:
+        indptr.append(indptr[-1] + n)
+    bt = w.block_table.cpu()
+    indices = torch.cat([bt[i, :n] for i, n in enumerate(npages)]).to(torch.int32)
+    last = torch.tensor([s - (n - 1) * bs if n else 0 for s, n in zip(lens_list, npages)],
+                        dtype=torch.int32)
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    wrapper = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD",
+                                                            use_tensor_cores=w.num_heads != w.num_kv_heads)
+    wrapper.plan(torch.tensor(indptr, dtype=torch.int32, device="cuda"), indices.cuda(),
+                 last.cuda(), w.num_heads, w.num_kv_heads, 128, bs, q_data_type=q.dtype,
+                 kv_data_type=k.dtype, sm_scale=scale)
+
+    def run():
+        return wrapper.run(q, (k, v))
+    return run, None
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--configs", default="c1,c2,c3,c4,c5")
+    ap.add_argument("--iters", type=int, default=50)
+    a = ap.parse_args()
+    flush = _Flush()
+    for name in a.configs.split(","):
+        w = workloads.CONFIGS[name]("cuda")
+        lens_list = w.seq_list()
+        lens = torch.tensor(lens_list, dtype=torch.int32, device="cuda")
+        max_s = max(lens_list)
+        scale = 1.0 / math.sqrt(128)
+        ws = pa.DecodeWorkspace("cuda")
+        mine_out = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                      w.block_size, workspace=ws)
+        res = {"config": w.name, "bytes": w.effective_bytes()}
+        res["this_us"] = _time(lambda: pa.paged_attention(w.q, w.k_cache, w.v_cache,
+                                                          w.block_table, w.seq_len, w.block_size,
+                                                          workspace=ws), flush, a.iters)
+        runners, err = _vllm_runners(w, lens, max_s, scale)
+        if err:
+            res["vllm"] = err
+        for key, fn in runners.items():
+            try:
+                o = fn().clone()
+                res[key + "_us"] = _time(fn, flush, a.iters)
+                res[key + "_matches"] = _close(o, mine_out)
+            except Exception as e:  # noqa: BLE001
+                res[key] = f"failed: {type(e).__name__}: {str(e)[:120]}"
+        try:
+            fi, err = _flashinfer_runner(w, lens_list, scale)
+            if err:
+                res["flashinfer"] = err
+            else:
+                o = fi().clone()
+                res["flashinfer_us"] = _time(fi, flush, a.iters)
+                res["flashinfer_matches"] = _close(o, mine_out)
+        except Exception as e:  # noqa: BLE001
+            res["flashinfer"] = f"failed: {type(e).__name__}: {str(e)[:120]}"
+        for key in list(res):
+            if key.endswith("_us"):
+                res[key.replace("_us", "_gbs")] = round(res["bytes"] / res[key] / 1e3, 1)
+                res[key] = round(res[key], 1)
+        print(json.dumps(res), flush=True)
+        del w
+
+
+if __name__ == "__main__":
+    main()
