@@ -425,6 +425,7 @@ def run_b200(args, rank, world, local_rank):
                 "us_per_step": round(e2e_mean * 1e3, 2),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "KV cache resident in HBM; q, block table (and lengths) in, O out"},
+        "capacity": capacity(w, eager_mean, dev),
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
@@ -435,6 +436,20 @@ def run_b200(args, rank, world, local_rank):
     if dist is not None:
         dist.destroy_process_group()
     return res
+
+
+def capacity(w, step_ms, dev):
+    """Layer-2 "paged architecture efficiency" figures (tests/benchmark_core.py:80-107)
+    for this workload on this device: KV bytes per request, decode tokens/s per GB
+    of KV, and how many such requests fit in 90 % of the device's memory (the
+    reference uses a fixed 8 GB budget)."""
+    e = w.q.element_size()
+    kv = sum(w.seq_list()) * w.num_kv_heads * 128 * e * 2
+    per_req = kv / w.batch
+    total = torch.cuda.get_device_properties(dev).total_memory
+    return {"kv_mb_per_request": round(per_req / 2**20, 2),
+            "tokens_per_s_per_gb": round(w.batch / (step_ms * 1e-3) / (kv / 1e9), 1),
+            "max_batch_in_90pct_hbm": int(0.9 * total // per_req)}
 
 
 # ----------------------------------------------------------------------------- CPU arm

@@ -109,6 +109,30 @@ PA_API pa_status_t pa_decode_workspace(const pa_decode_params* p, size_t* worksp
 /* Launch one decode step on `stream` (one kernel). */
 PA_API pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream);
 
+/* New tokens' K/V rows into the paged caches (the step before decode in a
+ * serving loop; the reference fills its caches in test code,
+ * tests/correctness.py:30-36). Row t of key/value ([num_tokens, num_kv_heads,
+ * head_dim], element strides, head_dim contiguous) goes to
+ * cache[slot / block_size, slot % block_size, :, :] with slot = slot_mapping[t];
+ * a negative slot skips the row (padding). A slot beyond the pool skips the row
+ * and ORs PA_STATUS_BAD_BLOCK into *status (when given). */
+typedef struct pa_append_params {
+  const void* key;
+  int64_t key_stride_t, key_stride_h;
+  const void* value;
+  int64_t value_stride_t, value_stride_h;
+  void* k_cache;
+  int64_t k_stride_block, k_stride_slot, k_stride_head;
+  void* v_cache;
+  int64_t v_stride_block, v_stride_slot, v_stride_head;
+  const int64_t* slot_mapping;   /* [num_tokens], device */
+  int32_t num_tokens, num_kv_heads, head_dim, block_size, num_blocks;
+  int32_t dtype;                 /* pa_dtype_t (element size 2) */
+  uint32_t* status;              /* optional device word */
+} pa_append_params;
+
+PA_API pa_status_t pa_cache_append(const pa_append_params* p, cudaStream_t stream);
+
 /* Allocation-free variant of pa_decode. It has no counterpart in the reference.
  *
  * pa_decode needs scratch memory (partial outputs of split segments and the

@@ -1119,6 +1119,47 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
 // ----------------------------------------------------------------------------
 // ----------------------------------------------------------------------------
+// KV-cache append: one thread per 16-byte chunk of a K or V row
+// ----------------------------------------------------------------------------
+struct AppendParams {
+  const char* key;
+  const char* value;
+  long long k_st, k_sh, v_st, v_sh;          // bytes
+  char* kc;
+  char* vc;
+  long long kc_sb, kc_ss, kc_sh, vc_sb, vc_ss, vc_sh;   // bytes
+  const long long* slots;
+  int T, Hkv, chunks, bs, NB;                // chunks: 16-byte pieces per row
+  unsigned* status;
+};
+
+__global__ void __launch_bounds__(256) cache_append_kernel(const AppendParams a) {
+  const long long per_tok = 2ll * a.Hkv * a.chunks;
+  const long long total = per_tok * a.T;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / per_tok);
+    long long r = i - t * per_tok;
+    const int is_v = static_cast<int>(r / (static_cast<long long>(a.Hkv) * a.chunks));
+    r -= static_cast<long long>(is_v) * a.Hkv * a.chunks;
+    const int h = static_cast<int>(r / a.chunks);
+    const int c = static_cast<int>(r - static_cast<long long>(h) * a.chunks);
+    const long long slot = __ldg(a.slots + t);
+    if (slot < 0) continue;
+    const long long blk = slot / a.bs;
+    const int off = static_cast<int>(slot - blk * a.bs);
+    if (blk >= a.NB) {
+      if (a.status && c == 0 && h == 0 && !is_v) atomicOr(a.status, PA_STATUS_BAD_BLOCK);
+      continue;
+    }
+    const char* src = is_v ? a.value + t * a.v_st + h * a.v_sh : a.key + t * a.k_st + h * a.k_sh;
+    char* dst = is_v ? a.vc + blk * a.vc_sb + off * a.vc_ss + h * a.vc_sh
+                     : a.kc + blk * a.kc_sb + off * a.kc_ss + h * a.kc_sh;
+    reinterpret_cast<uint4*>(dst)[c] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+  }
+}
+
+// ----------------------------------------------------------------------------
 // Bandwidth probes (replace measure_peak_bw.py:15-21's Triton copy kernel)
 // ----------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) stream_copy_kernel(const uint4* __restrict__ src,
@@ -1668,6 +1709,55 @@ pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t stream) {
   q.workspace = pl.ws_bytes ? base + counter_bytes : nullptr;
   q.workspace_bytes = pl.ws_bytes;
   return pa_decode(&q, stream);
+}
+
+pa_status_t pa_cache_append(const pa_append_params* p, cudaStream_t stream) {
+  if (!p) return PA_ERR_ARG;
+  if (p->num_tokens < 0 || p->num_kv_heads <= 0 || p->head_dim <= 0 || p->block_size <= 0 ||
+      p->num_blocks <= 0)
+    return PA_ERR_ARG;
+  if (p->dtype != PA_F16 && p->dtype != PA_BF16) return PA_ERR_ARG;
+  if (p->head_dim % 8) return PA_ERR_UNSUPPORTED;
+  if (p->num_tokens == 0) return PA_OK;
+  if (!p->key || !p->value || !p->k_cache || !p->v_cache || !p->slot_mapping) return PA_ERR_ARG;
+  if (!aligned16(p->key) || !aligned16(p->value) || !aligned16(p->k_cache) ||
+      !aligned16(p->v_cache))
+    return PA_ERR_ARG;
+  const int64_t strides[10] = {p->key_stride_t,   p->key_stride_h,   p->value_stride_t,
+                               p->value_stride_h, p->k_stride_block, p->k_stride_slot,
+                               p->k_stride_head,  p->v_stride_block, p->v_stride_slot,
+                               p->v_stride_head};
+  for (int i = 0; i < 10; ++i)
+    if (strides[i] % 8) return PA_ERR_ARG;
+  const int sms = sm_count(current_device());
+  if (sms <= 0) return PA_ERR_LAUNCH;
+  AppendParams a;
+  a.key = static_cast<const char*>(p->key);
+  a.value = static_cast<const char*>(p->value);
+  a.k_st = p->key_stride_t * 2;
+  a.k_sh = p->key_stride_h * 2;
+  a.v_st = p->value_stride_t * 2;
+  a.v_sh = p->value_stride_h * 2;
+  a.kc = static_cast<char*>(p->k_cache);
+  a.vc = static_cast<char*>(p->v_cache);
+  a.kc_sb = p->k_stride_block * 2;
+  a.kc_ss = p->k_stride_slot * 2;
+  a.kc_sh = p->k_stride_head * 2;
+  a.vc_sb = p->v_stride_block * 2;
+  a.vc_ss = p->v_stride_slot * 2;
+  a.vc_sh = p->v_stride_head * 2;
+  a.slots = reinterpret_cast<const long long*>(p->slot_mapping);
+  a.T = p->num_tokens;
+  a.Hkv = p->num_kv_heads;
+  a.chunks = p->head_dim / 8;
+  a.bs = p->block_size;
+  a.NB = p->num_blocks;
+  a.status = p->status;
+  const long long total = 2ll * p->num_tokens * p->num_kv_heads * a.chunks;
+  const long long want = (total + 255) / 256;
+  const int grid = static_cast<int>(std::min<long long>(want, 8ll * sms));
+  cache_append_kernel<<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 
 pa_status_t pa_stream_copy(const void* src, void* dst, size_t bytes, cudaStream_t stream) {

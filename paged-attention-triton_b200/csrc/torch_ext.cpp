@@ -157,9 +157,63 @@ std::tuple<int64_t, std::vector<at::Tensor>, int64_t, int64_t> decode(
   return {0, std::move(res), 0, 0};
 }
 
+// Writes key/value rows [T, Hkv, D] into the paged caches at slot_mapping[t]
+// (negative: skipped) through pa_cache_append.
+void cache_append(const at::Tensor& key, const at::Tensor& value, const at::Tensor& k_cache,
+                  const at::Tensor& v_cache, const at::Tensor& slot_mapping,
+                  const c10::optional<at::Tensor>& status) {
+  check(key.is_cuda() && value.is_cuda() && k_cache.is_cuda() && v_cache.is_cuda() &&
+            slot_mapping.is_cuda(),
+        "cache_append: all tensors must be CUDA tensors");
+  check(key.dim() == 3 && value.sizes() == key.sizes(), "key and value must be [T, Hkv, D]");
+  check(k_cache.dim() == 4 && v_cache.sizes() == k_cache.sizes(),
+        "caches must be [num_blocks, block_size, Hkv, D]");
+  check(key.size(1) == k_cache.size(2) && key.size(2) == k_cache.size(3),
+        "key rows and cache rows differ in Hkv or D");
+  const int dt = dtype_code(key);
+  check(value.scalar_type() == key.scalar_type() && k_cache.scalar_type() == key.scalar_type() &&
+            v_cache.scalar_type() == key.scalar_type(),
+        "key, value and caches must share one dtype");
+  check(slot_mapping.scalar_type() == at::kLong && slot_mapping.dim() == 1 &&
+            slot_mapping.size(0) == key.size(0) && slot_mapping.is_contiguous(),
+        "slot_mapping must be a contiguous int64 [T] tensor");
+  check(key.stride(2) == 1 && value.stride(2) == 1 && k_cache.stride(3) == 1 &&
+            v_cache.stride(3) == 1,
+        "head_dim must be contiguous");
+  c10::cuda::CUDAGuard guard(key.device());
+  pa_append_params a{};
+  a.key = key.data_ptr();
+  a.key_stride_t = key.stride(0);
+  a.key_stride_h = key.stride(1);
+  a.value = value.data_ptr();
+  a.value_stride_t = value.stride(0);
+  a.value_stride_h = value.stride(1);
+  a.k_cache = k_cache.data_ptr();
+  a.k_stride_block = k_cache.stride(0);
+  a.k_stride_slot = k_cache.stride(1);
+  a.k_stride_head = k_cache.stride(2);
+  a.v_cache = v_cache.data_ptr();
+  a.v_stride_block = v_cache.stride(0);
+  a.v_stride_slot = v_cache.stride(1);
+  a.v_stride_head = v_cache.stride(2);
+  a.slot_mapping = slot_mapping.data_ptr<int64_t>();
+  a.num_tokens = static_cast<int32_t>(key.size(0));
+  a.num_kv_heads = static_cast<int32_t>(key.size(1));
+  a.head_dim = static_cast<int32_t>(key.size(2));
+  a.block_size = static_cast<int32_t>(k_cache.size(1));
+  a.num_blocks = static_cast<int32_t>(k_cache.size(0));
+  a.dtype = dt;
+  a.status = status.has_value() ? reinterpret_cast<uint32_t*>(status->data_ptr<int32_t>())
+                                : nullptr;
+  const pa_status_t rc =
+      pa_cache_append(&a, c10::cuda::getCurrentCUDAStream(key.device().index()).stream());
+  TORCH_CHECK(rc == PA_OK, "pa_cache_append failed: ", pa_status_string(rc));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_pa_ext, m) {
+  m.def("cache_append", &cache_append, "write K/V rows into the paged caches by slot");
   m.doc() = "PyTorch binding of the sm_100a paged-attention decode C ABI";
   m.def("decode", &decode, "one paged-attention decode step (see torch_kernel.py)");
 }

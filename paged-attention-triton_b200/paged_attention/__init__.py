@@ -12,6 +12,7 @@ from .torch_kernel import (  # noqa: F401
     device_sm_count,
 )
 from .graph_runner import PagedAttnGraphRunner  # noqa: F401
+from .cache_ops import write_kv_cache, slots_for_positions  # noqa: F401
 from .split_kv_kernel import LSE_SENTINEL, LSE_VALID_THRESHOLD  # noqa: F401
 
 __all__ = ["paged_attention", "PagedAttnGraphRunner"]

@@ -73,6 +73,35 @@ class DecodeParams(ctypes.Structure):
     ]
 
 
+class AppendParams(ctypes.Structure):
+    """Mirror of ``pa_append_params``."""
+
+    _fields_ = [
+        ("key", ctypes.c_void_p),
+        ("key_stride_t", ctypes.c_int64),
+        ("key_stride_h", ctypes.c_int64),
+        ("value", ctypes.c_void_p),
+        ("value_stride_t", ctypes.c_int64),
+        ("value_stride_h", ctypes.c_int64),
+        ("k_cache", ctypes.c_void_p),
+        ("k_stride_block", ctypes.c_int64),
+        ("k_stride_slot", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("v_cache", ctypes.c_void_p),
+        ("v_stride_block", ctypes.c_int64),
+        ("v_stride_slot", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("slot_mapping", ctypes.c_void_p),
+        ("num_tokens", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("num_blocks", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/pa_decode.h.
 _SIGNATURES = {
     "pa_decode_workspace": (ctypes.c_int, [ctypes.POINTER(DecodeParams),
@@ -80,6 +109,7 @@ _SIGNATURES = {
                                            ctypes.POINTER(ctypes.c_size_t)]),
     "pa_decode": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
     "pa_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
+    "pa_cache_append": (ctypes.c_int, [ctypes.POINTER(AppendParams), ctypes.c_void_p]),
     "pa_num_splits_heuristic": (ctypes.c_int32, [ctypes.c_int32] * 5),
     "pa_stream_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.c_void_p]),

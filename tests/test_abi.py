@@ -24,7 +24,7 @@ def test_header_declares_expected_entry_points():
     names = set(_declared_functions())
     assert {"pa_decode", "pa_decode_workspace", "pa_num_splits_heuristic", "pa_stream_copy",
             "pa_stream_read", "pa_device_sm_count", "pa_status_string",
-            "pa_abi_version"} <= names
+            "pa_abi_version", "pa_cache_append"} <= names
 
 
 def test_library_exports_every_declared_symbol():
@@ -42,15 +42,18 @@ def test_library_has_no_cudart_runtime_dependency():
     assert "libcudart" not in out and "libcuda.so" not in out
 
 
-def test_struct_layout_matches_header(tmp_path):
+@pytest.mark.parametrize("cname,pyname", [("pa_decode_params", "DecodeParams"),
+                                          ("pa_append_params", "AppendParams")])
+def test_struct_layout_matches_header(tmp_path, cname, pyname):
     gcc = shutil.which("gcc")
     if not gcc:
         pytest.skip("gcc not available")
-    fields = [f[0] for f in _native.DecodeParams._fields_]
+    cls = getattr(_native, pyname)
+    fields = [f[0] for f in cls._fields_]
     src = ['#include <stdio.h>', '#include <stddef.h>', '#include "pa_decode.h"',
-           'int main(void) {', 'printf("size %zu\\n", sizeof(pa_decode_params));']
+           'int main(void) {', f'printf("size %zu\\n", sizeof({cname}));']
     for f in fields:
-        src.append(f'printf("{f} %zu\\n", offsetof(pa_decode_params, {f}));')
+        src.append(f'printf("{f} %zu\\n", offsetof({cname}, {f}));')
     src += ["return 0;", "}"]
     c = tmp_path / "probe.c"
     c.write_text("\n".join(src))
@@ -60,9 +63,9 @@ def test_struct_layout_matches_header(tmp_path):
                     str(exe)], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout
     got = dict(line.split() for line in out.strip().splitlines())
-    assert int(got["size"]) == ctypes.sizeof(_native.DecodeParams)
+    assert int(got["size"]) == ctypes.sizeof(cls)
     for f in fields:
-        assert int(got[f]) == getattr(_native.DecodeParams, f).offset, f
+        assert int(got[f]) == getattr(cls, f).offset, f
 
 
 @pytest.mark.parametrize("b,h,s,bs,sm", [(1, 32, 128, 16, 148), (32, 32, 1024, 16, 148),
