@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 INCLUDE = os.path.join(REPO, "include")
 SOURCES = [os.path.join(HERE, "csrc", "pa_decode.cu")]
-HEADERS = [os.path.join(INCLUDE, "pa_decode.h")]
+HEADERS = [os.path.join(INCLUDE, "pa_decode.h"), os.path.join(HERE, "csrc", "fastdiv.h")]
 OUTPUT = os.path.join(HERE, "paged_attention", "libpa_decode.so")
 EXT_SOURCE = os.path.join(HERE, "csrc", "torch_ext.cpp")
 EXT_OUTPUT = os.path.join(HERE, "paged_attention", "_pa_ext.so")

@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "pa_decode.h"
+#include "fastdiv.h"
 
 namespace pa {
 
@@ -93,6 +94,17 @@ struct KParams {
   int use_cum;              // balanced + seq_lens: prefix sums in shared memory
   int slot_cols;            // partial slot width: min(G, 8) query heads
   int gsz;                  // warps per merge group (NW, or 1 when the slots do not fit)
+  int zero_rows;            // 1: some row may have length 0 (the output pre-pass runs)
+  // Balanced schedule, computed on the host: the unit count and range sizes
+  // (valid when every row has the same length), and the launch-invariant
+  // divisors of the unit decode as multiply-shift constants.
+  int U, P, Pw;             // units; units per group range; per warp range
+  int nt_u, per_row;        // tiles per segment, units per row (same-length rows)
+  FastDiv div_row;          // by per_row
+  FastDiv div_nt;           // by nt_u
+  FastDiv div_qc;           // by QC
+  FastDiv div_bs;           // by bs (pages that are not a power of two)
+  FastDiv div_ng;           // by the number of groups (P with per-row lengths)
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -320,17 +332,17 @@ __device__ __forceinline__ void decode_unit(Cursor& c, const KParams& p, const i
     c.b = find_row(cum, p.B, u);
     row_base = cum[c.b];
     c.S = row_len(p, c.b);
+    c.nt = (c.S + TILE - 1) / TILE;
   } else {
     c.S = p.seq_len;
-    const int per_row = p.Hkv * p.QC * ((c.S + TILE - 1) / TILE);
-    c.b = u / per_row;
-    row_base = c.b * per_row;
+    c.nt = p.nt_u;
+    c.b = static_cast<int>(fast_div(static_cast<uint32_t>(u), p.div_row));
+    row_base = c.b * p.per_row;
   }
-  c.nt = (c.S + TILE - 1) / TILE;
   const int r = u - row_base;
-  const int seg = r / c.nt;
+  const int seg = p.use_cum ? r / c.nt : static_cast<int>(fast_div(static_cast<uint32_t>(r), p.div_nt));
   c.tile = r - seg * c.nt;
-  c.kvh = seg / p.QC;
+  c.kvh = p.QC == 1 ? seg : static_cast<int>(fast_div(static_cast<uint32_t>(seg), p.div_qc));
   c.qc = seg - c.kvh * p.QC;
   c.seg_lo = row_base + seg * c.nt;
 }
@@ -408,7 +420,8 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
     }
     const int tt = tile * TILE + j * p.R;
     if (tt < t1 && tt + p.R > t0) {
-      const int lp = p.bs_log2 >= 0 ? (tt >> p.bs_log2) : tt / p.bs;
+      const int lp = p.bs_log2 >= 0 ? (tt >> p.bs_log2)
+                                    : static_cast<int>(fast_div(static_cast<uint32_t>(tt), p.div_bs));
       off = static_cast<long long>(b) * p.bt_sb + lp;
       slot = tt - lp * p.bs;
     }
@@ -590,6 +603,10 @@ __global__ void __launch_bounds__(NW * 32, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < NW) gcnt[threadIdx.x] = 0;
+  // The warp's own barriers are initialised before any of its lanes issues a
+  // copy; the CTA-wide barrier that publishes gcnt comes after the first
+  // copies are in flight.
+  __syncwarp();
 
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
   if (p.ns == 0 && p.use_cum) {
@@ -622,11 +639,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
       run += nseg * ((S + TILE - 1) / TILE);
     }
     if (threadIdx.x == blockDim.x - 1) cum[B] = before + incl;
+    __syncthreads();
   }
-  __syncthreads();
 
   // Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
-  if (p.ns == 0) {
+  if (p.ns == 0 && p.zero_rows) {
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (row_len(p, b) != 0) continue;
       for (int idx = threadIdx.x; idx < p.Hq * (kD / 8); idx += blockDim.x) {
@@ -650,12 +667,19 @@ __global__ void __launch_bounds__(NW * 32, 1)
   w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
   int n_tiles = 0;
   if (p.ns == 0) {
-    rg.U = p.use_cum ? cum[p.B] : p.B * p.Hkv * p.QC * ((p.seq_len + TILE - 1) / TILE);
-    const int ngroups = gridDim.x * NW / p.gsz;
-    rg.P = max((rg.U + ngroups - 1) / ngroups, p.gsz);
-    rg.Pw = (rg.P + p.gsz - 1) / p.gsz;
-    rg.g = wid / p.gsz;
-    rg.gi = wid - rg.g * p.gsz;
+    if (p.use_cum) {
+      rg.U = cum[p.B];
+      rg.P = max(static_cast<int>(fast_div(static_cast<uint32_t>(rg.U) + p.div_ng.d - 1, p.div_ng)),
+                 p.gsz);
+      rg.Pw = p.gsz == 1 ? rg.P : (rg.P + NW - 1) / NW;
+    } else {
+      rg.U = p.U;
+      rg.P = p.P;
+      rg.Pw = p.Pw;
+    }
+    // groups are whole CTAs (gsz == NW) or single warps (gsz == 1)
+    rg.g = p.gsz == 1 ? wid : static_cast<int>(blockIdx.x);
+    rg.gi = p.gsz == 1 ? 0 : warp;
     rg.gr0 = min(rg.U, rg.g * rg.P);
     rg.gr1 = min(rg.U, rg.gr0 + rg.P);
     rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
@@ -790,6 +814,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   };
 
   for (int s = 0; s < NS && issued < n_tiles; ++s) issue(s);
+  if (p.ns == 0) __syncthreads();   // gcnt is zero for every warp's merges
 
   // ---- consumer state
   uint32_t qf[8][2];
@@ -1634,6 +1659,20 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.use_cum = pl.use_cum ? 1 : 0;
   kp.slot_cols = pl.slot_cols;
   kp.gsz = pl.gsz;
+  kp.zero_rows = (p->seq_lens != nullptr || p->seq_len == 0) ? 1 : 0;
+  if (pl.ns == 0) {
+    const int ngroups = pl.W / pl.gsz;
+    kp.nt_u = p->seq_lens ? 0 : (p->seq_len + tile - 1) / tile;
+    kp.per_row = p->num_kv_heads * pl.QC * kp.nt_u;
+    kp.U = p->batch * kp.per_row;            // fits int32: checked by make_plan
+    kp.P = std::max((kp.U + ngroups - 1) / ngroups, pl.gsz);
+    kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
+    kp.div_row = make_fastdiv(static_cast<uint32_t>(kp.per_row));
+    kp.div_nt = make_fastdiv(static_cast<uint32_t>(kp.nt_u));
+    kp.div_ng = make_fastdiv(static_cast<uint32_t>(ngroups));
+  }
+  kp.div_qc = make_fastdiv(static_cast<uint32_t>(pl.QC));
+  kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
 
   CUtensorMap mk, mv;
   kp.map5d = 1;
