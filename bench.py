@@ -10,9 +10,14 @@ step. One step = one decode call over the whole batch.
 
 Metric: effective KV HBM bandwidth in GB/s (K+V bytes of every cached token
 plus q and o bytes, divided by the step's device time) and decode-step us.
-L2 (126 MB) is flushed before every timed step by writing a 512 MB buffer and
-then reading another 512 MB buffer (so no dirty flush lines are left in L2);
-each step is bracketed by CUDA events on the launching stream.
+Timing is on the launching stream with CUDA events. When a rank's resident
+inputs exceed twice the L2 (126 MB; the default workload holds 537 MB) the K
+timed steps run back to back between one event pair (the reference's Layer-3
+method, ``tests/benchmark_core.py:133-145``), every step streaming its inputs
+from HBM; otherwise L2 is flushed before every timed step by writing a 512 MB
+buffer and then reading another 512 MB buffer (so no dirty flush lines are left
+in L2) and each step has its own event pair. Per-step, L2-flushed timings are
+reported beside the headline either way.
 
 Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): weak scaling by
 KV head -- rank r holds its own 32-KV-head shard (own seeded pool and block
@@ -48,6 +53,7 @@ import torch  # noqa: E402
 METRIC = ("decode-step µs and effective KV HBM GB/s (% of B200 peak), eager+graph, "
           "1/2/4/8 GPU")
 FLUSH_BYTES = 512 * 1024 * 1024
+L2_BYTES = 126 * 1024 * 1024
 PROFILE_TRAFFIC = os.path.join(ROOT, "profiles", "pa_decode_c2_traffic.txt")
 
 
@@ -253,23 +259,48 @@ def run_b200(args, rank, world, local_rank):
     err = (out.float().cpu()[idx] - ro[idx]).abs()
     parity_ok = bool((err <= 2e-3 + 1e-2 * ro[idx].abs()).all())
 
-    # ---- eager, device-timed, L2 flushed before every step
-    for _ in range(args.warmup):
-        flusher()
-        op()
-    barrier()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(dev.index) as clocks:
+    # Inputs larger than twice the L2 stream from HBM in every step: time the
+    # steps back to back. Smaller ones get the L2 flushed before every step.
+    back_to_back = nbytes > 2 * L2_BYTES
+
+    def timed(fn, flush, steps):
+        """Per-step events around every step."""
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         barrier()
-        for k in range(args.steps):
-            flusher()
+        for k in range(steps):
+            if flush:
+                flusher()
             starts[k].record(stream)
-            op()
+            fn()
             ends[k].record(stream)
         barrier()
-    eager_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    eager = _stats(eager_ms)
+        return _stats([s.elapsed_time(e) for s, e in zip(starts, ends)])
+
+    def timed_back_to_back(fn, steps):
+        """One event pair around `steps` consecutive steps (nothing between the
+        launches, as in steady-state decoding); mean = elapsed / steps."""
+        s_ev = torch.cuda.Event(enable_timing=True)
+        e_ev = torch.cuda.Event(enable_timing=True)
+        barrier()
+        s_ev.record(stream)
+        for _ in range(steps):
+            fn()
+        e_ev.record(stream)
+        barrier()
+        mean = s_ev.elapsed_time(e_ev) / steps
+        return {"mean": mean, "median": mean, "min": mean, "max": mean}
+
+    # ---- eager, device-timed (the headline)
+    for _ in range(args.warmup):
+        if not back_to_back:
+            flusher()
+        op()
+    barrier()
+    with ClockSampler(dev.index) as clocks:
+        eager = timed_back_to_back(op, args.steps) if back_to_back else timed(op, True, args.steps)
+    # the same steps with L2 flushed before each (reported beside the headline)
+    eager_flushed = eager if not back_to_back else timed(op, True, args.steps)
 
     # ---- graph replay (one kernel node), same flush discipline
     runner = pa.PagedAttnGraphRunner(w.batch, w.num_heads, 128, max(w.seq_list()), w.block_size,
@@ -347,23 +378,18 @@ def run_b200(args, rank, world, local_rank):
         o_host.copy_(o, non_blocking=True)
 
     for _ in range(args.warmup):
-        flusher()
+        if not back_to_back:
+            flusher()
         e2e_step()
     barrier()
-    es = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ee = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for k in range(args.steps):
-        flusher()
-        es[k].record(stream)
-        e2e_step()
-        ee[k].record(stream)
-    barrier()
-    e2e = _stats([s.elapsed_time(e) for s, e in zip(es, ee)])
+    e2e = timed_back_to_back(e2e_step, args.steps) if back_to_back else timed(e2e_step, True,
+                                                                               args.steps)
     e2e_ok = torch.equal(o_host, out.cpu())
 
     # ---- max over ranks
-    eager_mean, graph_mean, e2e_mean, sync_med, graph_b2b = max_over_ranks(
-        [eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"], graph_b2b_ms], dist, dev)
+    eager_mean, graph_mean, e2e_mean, sync_med, graph_b2b, flushed_mean = max_over_ranks(
+        [eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"], graph_b2b_ms,
+         eager_flushed["mean"]], dist, dev)
 
     # ---- verification all-gather over NCCL (outside the timed region)
     if dist is not None:
@@ -402,14 +428,20 @@ def run_b200(args, rank, world, local_rank):
             "head_dim": 128, "block_size": w.block_size,
             "seq_len": w.seq_len if isinstance(w.seq_len, int) else "per-row",
             "kv_bytes_per_rank": nbytes,
-            "l2": "flushed before every step: 512 MB write, then 512 MB read (no dirty lines left)",
+            "l2": (f"inputs {nbytes / 1e6:.0f} MB per rank > 2x L2 (126 MB): the K steps run back "
+                   "to back between one event pair, each streaming its inputs from HBM "
+                   "(per-step-event timings with L2 flushed under us_per_step)"
+                   if back_to_back else
+                   "flushed before every step: 512 MB write, then 512 MB read (no dirty lines left)"),
             "schedule": "token-balanced persistent",
             "parallelism": (f"kv-head shards x{world}" if world > 1 else "single GPU"),
         },
-        "us_per_step": {"eager": round(eager_mean * 1e3, 2), "graph": round(graph_mean * 1e3, 2),
+        "us_per_step": {"eager": round(eager_mean * 1e3, 2),
+                        "eager_l2_flushed": round(flushed_mean * 1e3, 2),
+                        "graph_l2_flushed": round(graph_mean * 1e3, 2),
                         "eager_host_sync": round(sync_med * 1e3, 2),
                         "graph_back_to_back": round(graph_b2b * 1e3, 2),
-                        "eager_median": round(eager["median"] * 1e3, 2),
+                        "eager_l2_flushed_median": round(eager_flushed["median"] * 1e3, 2),
                         "graph_median": round(graph["median"] * 1e3, 2)},
         "graph_gbs": round(total_bytes / (graph_mean * 1e-3) / 1e9, 1),
         "pct_of_peak": {"eager": round(100 * value / world / peak, 1),

@@ -454,8 +454,38 @@ __device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, floa
     const float4* r4 = reinterpret_cast<const float4*>(row) + lane;
     return kGlobal ? __ldcg(r4) : *r4;
   };
-  const float l0 = (lane < n) ? ld_lse(lane) : kValidLse;
   float4 v[kBatch];
+  if (n <= kBatch) {
+    // At most one batch (the shared-memory merges and most group merges): one
+    // straight pass, every lane reading all LSEs (a broadcast) and its float4
+    // of every row; no loops or shuffles on the tail of the step.
+    float l[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      l[u] = (u < n) ? ld_lse(u) : kSentinel;
+      v[u] = (u < n) ? ld_row(u) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float gmax = kValidLse;
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (l[u] > kValidLse) gmax = fmaxf(gmax, l[u]);
+    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float gsum = 0.f;
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const float wgt = (l[u] > kValidLse) ? exp2f((l[u] - gmax) * kLog2e) : 0.f;
+      gsum += wgt;
+      a4.x = fmaf(wgt, v[u].x, a4.x);
+      a4.y = fmaf(wgt, v[u].y, a4.y);
+      a4.z = fmaf(wgt, v[u].z, a4.z);
+      a4.w = fmaf(wgt, v[u].w, a4.w);
+    }
+    const float inv = __fdividef(1.f, fmaxf(gsum, 1e-20f));
+    out4 = make_float4(a4.x * inv, a4.y * inv, a4.z * inv, a4.w * inv);
+    lse_out = gsum > 0.f ? gmax + __logf(gsum) : kSentinel;
+    return;
+  }
+  const float l0 = (lane < n) ? ld_lse(lane) : kValidLse;
 #pragma unroll
   for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? ld_row(u) : make_float4(0.f, 0.f, 0.f, 0.f);
   float gmax = (l0 > kValidLse) ? l0 : kValidLse;
@@ -608,6 +638,30 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // copies are in flight.
   __syncwarp();
 
+  // ---------------------------------------------------------------- schedule
+  const int wid = blockIdx.x * NW + warp;
+  Ranges rg;
+  rg.U = rg.P = rg.Pw = rg.g = rg.gi = rg.gr0 = rg.gr1 = rg.wr0 = rg.wr1 = 0;
+  auto set_ranges = [&](int U, int P, int Pw) {
+    rg.U = U;
+    rg.P = P;
+    rg.Pw = Pw;
+    // groups are whole CTAs (gsz == NW) or single warps (gsz == 1)
+    rg.g = p.gsz == 1 ? wid : static_cast<int>(blockIdx.x);
+    rg.gi = p.gsz == 1 ? 0 : warp;
+    rg.gr0 = min(rg.U, rg.g * rg.P);
+    rg.gr1 = min(rg.U, rg.gr0 + rg.P);
+    rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
+    rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
+  };
+  // Same-length rows: the ranges need no memory, so they are set before the wait.
+  if (p.ns == 0 && !p.use_cum) set_ranges(p.U, p.P, p.Pw);
+
+  // Programmatic dependent launch: everything above touches no global memory;
+  // from here on the kernel reads inputs (and writes outputs, partials and
+  // counters) that the previous kernel in the stream may still be using.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
   if (p.ns == 0 && p.use_cum) {
     const int B = p.B;
@@ -656,34 +710,20 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
   }
 
-  // ---------------------------------------------------------------- schedule
-  const int wid = blockIdx.x * NW + warp;
   const int G = p.G;
   const int spt_mask = (1 << p.lspt) - 1;
   const int bt_tiles = 32 >> p.lspt;          // tiles per page batch (one box per lane)
-  Ranges rg;
-  rg.U = rg.P = rg.Pw = rg.g = rg.gi = rg.gr0 = rg.gr1 = rg.wr0 = rg.wr1 = 0;
   Work w;
   w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
   int n_tiles = 0;
   if (p.ns == 0) {
     if (p.use_cum) {
-      rg.U = cum[p.B];
-      rg.P = max(static_cast<int>(fast_div(static_cast<uint32_t>(rg.U) + p.div_ng.d - 1, p.div_ng)),
-                 p.gsz);
-      rg.Pw = p.gsz == 1 ? rg.P : (rg.P + NW - 1) / NW;
-    } else {
-      rg.U = p.U;
-      rg.P = p.P;
-      rg.Pw = p.Pw;
+      const int U = cum[p.B];
+      const int P = max(static_cast<int>(fast_div(static_cast<uint32_t>(U) + p.div_ng.d - 1,
+                                                  p.div_ng)),
+                        p.gsz);
+      set_ranges(U, P, p.gsz == 1 ? P : (P + NW - 1) / NW);
     }
-    // groups are whole CTAs (gsz == NW) or single warps (gsz == 1)
-    rg.g = p.gsz == 1 ? wid : static_cast<int>(blockIdx.x);
-    rg.gi = p.gsz == 1 ? 0 : warp;
-    rg.gr0 = min(rg.U, rg.g * rg.P);
-    rg.gr1 = min(rg.U, rg.gr0 + rg.P);
-    rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
-    rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
     n_tiles = rg.wr1 - rg.wr0;
   } else {
     const int total = p.B * p.Hkv * p.QC * p.ns;
@@ -740,7 +780,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
   int u0n = u1c, u1n = min(range1, u1c + bt_tiles);
   int pg_c = INT_MIN, sl_c = 0, pg_n = INT_MIN, sl_n = 0;
   if (u0c < u1c) batch_pages<TILE>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
-  if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   Cursor ic;
   ic.b = w.b;
   ic.kvh = w.kvh;
@@ -814,7 +853,15 @@ __global__ void __launch_bounds__(NW * 32, 1)
   };
 
   for (int s = 0; s < NS && issued < n_tiles; ++s) issue(s);
+  // The second batch's block-table loads leave the path to the first copies: a
+  // batch holds at least 8 tiles (32 boxes of >= 8 rows), more than the NS
+  // issued above, so those never reached it (a range that ended inside the
+  // first batch has no second one).
+  if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   if (p.ns == 0) __syncthreads();   // gcnt is zero for every warp's merges
+  // The next kernel in the stream may start its own prologue on SMs this grid
+  // leaves; it waits for this grid's completion before touching memory.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---- consumer state
   uint32_t qf[8][2];
@@ -1052,8 +1099,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (c >= gc) continue;
       const int hq = kvh * G + qc * 8 + c;
       const float lv = fmaxf(lsum[e], 1e-20f);
-      const float inv_l = 1.f / lv;
-      const float lse = (m_run[e] * scl + log2f(lv)) * kLn2;
+      const float inv_l = __fdividef(1.f, lv);
+      const float lse = (m_run[e] * scl + __log2f(lv)) * kLn2;
       if (dest == 0) {
         char* dst = p.out + b * p.o_sb + hq * p.o_sh;
 #pragma unroll
@@ -1517,8 +1564,20 @@ static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUten
       attr_set[dev] = true;
     }
   }
-  pa_decode_kernel<T, kDup, TILE, NW, NS><<<pl.grid, NW * 32, pl.smem, stream>>>(mk, mv, kp);
-  return cudaGetLastError();
+  // Programmatic stream serialisation: the grid may be scheduled while the
+  // previous kernel in the stream finishes; the kernel's griddepcontrol.wait
+  // orders all of its memory accesses after that kernel.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS>, mk, mv, kp);
 }
 
 template <typename T, bool kDup>
