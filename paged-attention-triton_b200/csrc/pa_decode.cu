@@ -1725,6 +1725,16 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
     kp.per_row = p->num_kv_heads * pl.QC * kp.nt_u;
     kp.U = p->batch * kp.per_row;            // fits int32: checked by make_plan
     kp.P = std::max((kp.U + ngroups - 1) / ngroups, pl.gsz);
+    // Whole segments per group when that costs at most 3 % of balance: no
+    // segment then crosses a group, so no piece needs the global merge (its
+    // fence, atomic and extra round trip land on one warp of the group and
+    // make that warp the group's last).
+    const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
+    if (kp.nt_u > 0 && nseg_total >= ngroups) {
+      const long long aligned = (nseg_total + ngroups - 1) / ngroups * kp.nt_u;
+      if (aligned * 100 <= static_cast<long long>(kp.P) * 103 && aligned >= pl.gsz)
+        kp.P = static_cast<int>(aligned);
+    }
     kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
     kp.div_row = make_fastdiv(static_cast<uint32_t>(kp.per_row));
     kp.div_nt = make_fastdiv(static_cast<uint32_t>(kp.nt_u));
