@@ -43,7 +43,7 @@ extern "C" {
 typedef enum pa_status {
   PA_OK = 0,
   PA_ERR_ARG = 1,          /* null pointer, inconsistent shape, bad stride/alignment */
-  PA_ERR_UNSUPPORTED = 2,  /* legal but not built: head_dim != 128, block_size % 8 != 0 */
+  PA_ERR_UNSUPPORTED = 2,  /* legal but not built: head_dim not 64/128/256, block_size % 8 != 0 */
   PA_ERR_LAUNCH = 3,       /* CUDA runtime/driver error while launching */
   PA_ERR_WORKSPACE = 4     /* workspace or counter buffer smaller than queried */
 } pa_status_t;
@@ -96,8 +96,10 @@ typedef struct pa_decode_params {
   int32_t* counters;           /* zero-filled once by the caller; the kernel leaves it zeroed */
   size_t counter_count;
   uint32_t* status;            /* optional device word, PA_STATUS_* bits OR-ed in */
-  /* 0: automatic. 1..5: a fixed kernel variant (tile tokens x warps x ring
-   * depth), for tuning; see the variant table in csrc/pa_decode.cu. */
+  /* 0: automatic. 1..7: a fixed kernel variant (tile tokens x warps x ring
+   * depth), for tuning; see the variant table in csrc/pa_decode.cu (1-5 for
+   * head_dim 128, 3 and 5 for 64, 6 and 7 for 256; others return
+   * PA_ERR_UNSUPPORTED). */
   int32_t kernel_variant;
 } pa_decode_params;
 

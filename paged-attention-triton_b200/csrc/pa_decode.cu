@@ -36,10 +36,8 @@
 
 namespace pa {
 
-constexpr int kD = 128;             // head_dim
 constexpr int kCumMax = 1024;       // rows whose tile prefix sum fits in shared memory
 constexpr int kDescInts = 12;       // per-stage tile descriptor
-constexpr int kSlotStride = 132;    // floats per merge row in shared memory (128 + LSE, 16-B aligned)
 constexpr float kSentinel = -1e30f;     // split_kv_kernel.py:8
 constexpr float kValidLse = -1e29f;     // split_kv_kernel.py:9
 constexpr float kLog2e = 1.4426950408889634f;
@@ -47,14 +45,25 @@ constexpr float kLn2 = 0.6931471805599453f;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s per barrier wait
 constexpr unsigned kFull = 0xffffffffu;
 
+// Head-dimension constants (D in {64, 128, 256}).
+template <int D>
+struct HD {
+  static constexpr int kChunks = D / 64;       // 128-byte (64-dim) chunks of one K/V row
+  static constexpr int kSteps = D / 16;        // 16-dim MMA steps over a row
+  static constexpr int kLaneF = D / 32;        // floats of a merge row held by one lane
+  static constexpr int kSlotStride = D + 4;    // floats per shared merge row (D + LSE, 16-B aligned)
+};
+
 // Shared-memory plan of one kernel variant.
-template <bool kDup, int TILE, int NW, int NS>
+template <bool kDup, int TILE, int NW, int NS, int D>
 struct Cfg {
   static constexpr int kMB = TILE / 16;            // 16-token m-blocks per tile
   // A K (or V) tile is stored box-major: for each TMA box of R token rows,
-  // [half 0: R rows x 128 B][half 1: R rows x 128 B], each half 128-byte swizzled.
-  static constexpr int kKV = TILE * 256;           // one K (or V) tile
-  static constexpr int kQ = kDup ? 1024 : 2048;    // query rows loaded with a piece's first tile
+  // [chunk 0: R rows x 128 B]...[chunk D/64-1], each chunk 128-byte swizzled.
+  static constexpr int kKV = TILE * D * 2;         // one K (or V) tile
+  // query rows loaded with a piece's first tile (4 heads with duplicated
+  // columns, else 8), rounded to the 1 KB swizzle atom
+  static constexpr int kQ = ((kDup ? 4 : 8) * D * 2 + 1023) / 1024 * 1024;
   static constexpr int kStage = 2 * kKV + kQ;      // multiple of 1 KB (swizzle atom)
   static constexpr int kStagesBytes = NW * NS * kStage;
   static constexpr int kBarOff = kStagesBytes;
@@ -64,7 +73,7 @@ struct Cfg {
   static constexpr int kGroupOff = (kCumOff + (kCumMax + 1) * 4 + 15) & ~15;
   static constexpr int kGroupCntBytes = (NW * 4 + 15) & ~15;
   static constexpr int kSmemBase = kGroupOff + kGroupCntBytes + 1024;  // + alignment slack
-  static constexpr int kGroupSlotBytes = NW * 2 * kSlotStride * 4;   // per slot column
+  static constexpr int kGroupSlotBytes = NW * 2 * HD<D>::kSlotStride * 4;   // per slot column
 };
 
 struct KParams {
@@ -432,14 +441,56 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
 // ----------------------------------------------------------------------------
 // Merging pieces
 // ----------------------------------------------------------------------------
+// One lane's share of a merge row: floats [lane * N, lane * N + N).
+template <int N>
+struct RowV {
+  float f[N];
+};
+
+template <bool kGlobal, int N>
+__device__ __forceinline__ RowV<N> load_row(const float* row, int lane) {
+  RowV<N> r;
+  const float* q = row + lane * N;
+  if constexpr (N == 2) {
+    const float2* q2 = reinterpret_cast<const float2*>(q);
+    const float2 t = kGlobal ? __ldcg(q2) : *q2;
+    r.f[0] = t.x;
+    r.f[1] = t.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4* q4 = reinterpret_cast<const float4*>(q + i);
+      const float4 t = kGlobal ? __ldcg(q4) : *q4;
+      r.f[i] = t.x;
+      r.f[i + 1] = t.y;
+      r.f[i + 2] = t.z;
+      r.f[i + 3] = t.w;
+    }
+  }
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ void store_row(float* row, int lane, const RowV<N>& r) {
+  float* q = row + lane * N;
+  if constexpr (N == 2) {
+    *reinterpret_cast<float2*>(q) = make_float2(r.f[0], r.f[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+      *reinterpret_cast<float4*>(q + i) = make_float4(r.f[i], r.f[i + 1], r.f[i + 2], r.f[i + 3]);
+  }
+}
+
 // split_kv_kernel.py:101-122: skip lse <= -1e29, merge by running max, divide
 // by max(sum, 1e-20); no valid piece gives 0 and LSE -1e30. `src(k, row, lse)`
-// locates piece k's normalised row (128 floats) and LSE; rows are read from
+// locates piece k's normalised row (D floats) and LSE; rows are read from
 // global memory through L2 (kGlobal) or from shared memory. Each lane returns
-// its 4 of the 128 dims.
-template <bool kGlobal, class Src>
-__device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, float4& out4,
-                                           float& lse_out) {
+// its D/32 dims.
+template <bool kGlobal, int D, class Src>
+__device__ __forceinline__ void merge_rows(int n, int lane, const Src& src,
+                                           RowV<HD<D>::kLaneF>& out, float& lse_out) {
+  constexpr int N = HD<D>::kLaneF;
   constexpr int kBatch = 8;   // rows in flight per lane
   auto ld_lse = [&](int k) {
     const float* row;
@@ -451,43 +502,44 @@ __device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, floa
     const float* row;
     const float* lp;
     src(k, row, lp);
-    const float4* r4 = reinterpret_cast<const float4*>(row) + lane;
-    return kGlobal ? __ldcg(r4) : *r4;
+    return load_row<kGlobal, N>(row, lane);
   };
-  float4 v[kBatch];
+  RowV<N> zero;
+#pragma unroll
+  for (int i = 0; i < N; ++i) zero.f[i] = 0.f;
+  RowV<N> v[kBatch];
+  RowV<N> a = zero;
   if (n <= kBatch) {
     // At most one batch (the shared-memory merges and most group merges): one
-    // straight pass, every lane reading all LSEs (a broadcast) and its float4
+    // straight pass, every lane reading all LSEs (a broadcast) and its share
     // of every row; no loops or shuffles on the tail of the step.
     float l[kBatch];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       l[u] = (u < n) ? ld_lse(u) : kSentinel;
-      v[u] = (u < n) ? ld_row(u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u] = (u < n) ? ld_row(u) : zero;
     }
     float gmax = kValidLse;
 #pragma unroll
     for (int u = 0; u < kBatch; ++u)
       if (l[u] > kValidLse) gmax = fmaxf(gmax, l[u]);
-    float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float gsum = 0.f;
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
       const float wgt = (l[u] > kValidLse) ? exp2f((l[u] - gmax) * kLog2e) : 0.f;
       gsum += wgt;
-      a4.x = fmaf(wgt, v[u].x, a4.x);
-      a4.y = fmaf(wgt, v[u].y, a4.y);
-      a4.z = fmaf(wgt, v[u].z, a4.z);
-      a4.w = fmaf(wgt, v[u].w, a4.w);
+#pragma unroll
+      for (int i = 0; i < N; ++i) a.f[i] = fmaf(wgt, v[u].f[i], a.f[i]);
     }
     const float inv = __fdividef(1.f, fmaxf(gsum, 1e-20f));
-    out4 = make_float4(a4.x * inv, a4.y * inv, a4.z * inv, a4.w * inv);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out.f[i] = a.f[i] * inv;
     lse_out = gsum > 0.f ? gmax + __logf(gsum) : kSentinel;
     return;
   }
   const float l0 = (lane < n) ? ld_lse(lane) : kValidLse;
 #pragma unroll
-  for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? ld_row(u) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int u = 0; u < kBatch; ++u) v[u] = (u < n) ? ld_row(u) : zero;
   float gmax = (l0 > kValidLse) ? l0 : kValidLse;
   for (int k = lane + 32; k < n; k += 32) {
     const float l = ld_lse(k);
@@ -495,7 +547,6 @@ __device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, floa
   }
 #pragma unroll
   for (int o2 = 16; o2 > 0; o2 >>= 1) gmax = fmaxf(gmax, __shfl_xor_sync(kFull, gmax, o2));
-  float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
   float gsum = 0.f;
   for (int base = 0; base < n; base += 32) {
     const float lb = (base == 0) ? l0 : ((base + lane < n) ? ld_lse(base + lane) : kValidLse);
@@ -509,45 +560,55 @@ __device__ __forceinline__ void merge_rows(int n, int lane, const Src& src, floa
       if (base + k0 > 0) {
 #pragma unroll
         for (int u = 0; u < kBatch; ++u)
-          v[u] = (k0 + u < cnt) ? ld_row(base + k0 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[u] = (k0 + u < cnt) ? ld_row(base + k0 + u) : zero;
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const float wgt = __shfl_sync(kFull, wl, (k0 + u) & 31);
         if (k0 + u < cnt && wgt > 0.f) {
-          a4.x = fmaf(wgt, v[u].x, a4.x);
-          a4.y = fmaf(wgt, v[u].y, a4.y);
-          a4.z = fmaf(wgt, v[u].z, a4.z);
-          a4.w = fmaf(wgt, v[u].w, a4.w);
+#pragma unroll
+          for (int i = 0; i < N; ++i) a.f[i] = fmaf(wgt, v[u].f[i], a.f[i]);
         }
       }
     }
   }
   const float inv = 1.f / fmaxf(gsum, 1e-20f);
-  out4 = make_float4(a4.x * inv, a4.y * inv, a4.z * inv, a4.w * inv);
+#pragma unroll
+  for (int i = 0; i < N; ++i) out.f[i] = a.f[i] * inv;
   lse_out = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
 }
 
-template <typename T>
-__device__ __forceinline__ void store_out4(const KParams& p, int b, int hq, int lane, float4 o,
-                                           float lse) {
-  char* dst = p.out + b * p.o_sb + hq * p.o_sh + lane * 8;
-  const uint32_t lo = pack16(Mma<T>::from_float(o.x), Mma<T>::from_float(o.y));
-  const uint32_t hi = pack16(Mma<T>::from_float(o.z), Mma<T>::from_float(o.w));
-  *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+// Final output row of (b, hq): this lane's D/32 dims in the output dtype.
+template <typename T, int D>
+__device__ __forceinline__ void store_out(const KParams& p, int b, int hq, int lane,
+                                          const RowV<HD<D>::kLaneF>& o, float lse) {
+  constexpr int N = HD<D>::kLaneF;
+  char* dst = p.out + b * p.o_sb + hq * p.o_sh + lane * N * 2;
+  uint32_t w[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i)
+    w[i] = pack16(Mma<T>::from_float(o.f[2 * i]), Mma<T>::from_float(o.f[2 * i + 1]));
+  if constexpr (N == 2) {
+    *reinterpret_cast<uint32_t*>(dst) = w[0];
+  } else if constexpr (N == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
   if (lane == 0 && p.lse) p.lse[b * p.Hq + hq] = lse;
 }
 
 // Global partial slot of group g's piece: row of column j.
+template <int D>
 __device__ __forceinline__ float* gslot_row(const KParams& p, long long slot, int j) {
-  return p.o_part + (slot * p.slot_cols + j) * kD;
+  return p.o_part + (slot * p.slot_cols + j) * D;
 }
 __device__ __forceinline__ float* gslot_lse(const KParams& p, long long slot, int j) {
   return p.lse_part + slot * p.slot_cols + j;
 }
 
 // The last group to finish a segment merges the groups' partials.
-template <typename T>
+template <typename T, int D>
 __device__ __forceinline__ void merge_groups(const KParams& p, const Ranges& rg, int b, int kvh,
                                              int qc, int gc, int seg_lo, int seg_hi, int lane) {
   const int g_first = seg_lo / rg.P;
@@ -556,37 +617,37 @@ __device__ __forceinline__ void merge_groups(const KParams& p, const Ranges& rg,
     auto src = [&](int k, const float*& row, const float*& lp) {
       const int g = g_first + k;
       const long long sl = 2ll * g + (max(seg_lo, g * rg.P) == g * rg.P ? 0 : 1);
-      row = gslot_row(p, sl, j);
+      row = gslot_row<D>(p, sl, j);
       lp = gslot_lse(p, sl, j);
     };
-    float4 o4;
+    RowV<HD<D>::kLaneF> o;
     float lse;
-    merge_rows<true>(n, lane, src, o4, lse);
-    store_out4<T>(p, b, kvh * p.G + qc * 8 + j, lane, o4, lse);
+    merge_rows<true, D>(n, lane, src, o, lse);
+    store_out<T, D>(p, b, kvh * p.G + qc * 8 + j, lane, o, lse);
   }
 }
 
 // Split schedule: the last split of a segment merges rows [b, hq, 0..ns).
-template <typename T>
+template <typename T, int D>
 __device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, int qc, int gc,
                                              int lane) {
   for (int j = 0; j < gc; ++j) {
     const int hq = kvh * p.G + qc * 8 + j;
     const long long row0 = (static_cast<long long>(b) * p.Hq + hq) * p.ns;
     auto src = [&](int k, const float*& row, const float*& lp) {
-      row = p.o_part + (row0 + k) * kD;
+      row = p.o_part + (row0 + k) * D;
       lp = p.lse_part + row0 + k;
     };
-    float4 o4;
+    RowV<HD<D>::kLaneF> o;
     float lse;
-    merge_rows<true>(p.ns, lane, src, o4, lse);
-    store_out4<T>(p, b, hq, lane, o4, lse);
+    merge_rows<true, D>(p.ns, lane, src, o, lse);
+    store_out<T, D>(p, b, hq, lane, o, lse);
   }
 }
 
 // Publishes the group's piece (already written to its global slot) and merges
 // the segment if this group arrived last.
-template <typename T>
+template <typename T, int D>
 __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg, int b, int kvh,
                                               int qc, int gc, int seg_lo, int seg_hi, int lane) {
   __threadfence();
@@ -598,18 +659,19 @@ __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg
   last = __shfl_sync(kFull, last, 0);
   if (!last) return;
   __threadfence();
-  merge_groups<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+  merge_groups<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
   if (lane == 0) atomicExch(p.counters + cid, 0);
 }
 
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
-template <typename T, bool kDup, int TILE, int NW, int NS>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D>
 __global__ void __launch_bounds__(NW * 32, 1)
     pa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const KParams p) {
-  using C = Cfg<kDup, TILE, NW, NS>;
+  using C = Cfg<kDup, TILE, NW, NS, D>;
+  using H = HD<D>;
   constexpr int kMB = C::kMB;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -700,8 +762,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   if (p.ns == 0 && p.zero_rows) {
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (row_len(p, b) != 0) continue;
-      for (int idx = threadIdx.x; idx < p.Hq * (kD / 8); idx += blockDim.x) {
-        const int h = idx / (kD / 8), c = idx % (kD / 8);
+      for (int idx = threadIdx.x; idx < p.Hq * (D / 8); idx += blockDim.x) {
+        const int h = idx / (D / 8), c = idx % (D / 8);
         *reinterpret_cast<uint4*>(p.out + b * p.o_sb + h * p.o_sh + c * 16) =
             make_uint4(0, 0, 0, 0);
       }
@@ -759,7 +821,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     for (int j = 0; j < gc; ++j) {
       const int hq = w.kvh * G + w.qc * 8 + j;
       const long long row = (static_cast<long long>(w.b) * p.Hq + hq) * p.ns + w.s;
-      for (int d = lane; d < kD; d += 32) p.o_part[row * kD + d] = 0.f;
+      for (int d = lane; d < D; d += 32) p.o_part[row * D + d] = 0.f;
       if (lane == 0) p.lse_part[row] = kSentinel;
     }
     __threadfence();
@@ -770,7 +832,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     last = __shfl_sync(kFull, last, 0);
     if (!last) return;
     __threadfence();
-    merge_splits<T>(p, w.b, w.kvh, w.qc, gc, lane);
+    merge_splits<T, D>(p, w.b, w.kvh, w.qc, gc, lane);
     if (lane == 0) atomicExch(p.counters + cid, 0);
     return;
   }
@@ -818,25 +880,27 @@ __global__ void __launch_bounds__(NW * 32, 1)
       reinterpret_cast<int4*>(d)[0] = make_int4(ic.b, ic.kvh, ic.qc, ic.tile * TILE);
       reinterpret_cast<int4*>(d)[1] = make_int4(t0, t1, ic.seg_lo, ic.seg_lo + ic.nt);
       reinterpret_cast<int4*>(d)[2] = make_int4(fl, gc, 0, 0);
-      mbar_expect_tx(bar, __popc(vm) * 4 * p.R * 128 + (first ? gc * kD * 2 : 0));
+      // per box: K and V, D/64 chunks of R rows x 128 B each; plus the query rows
+      mbar_expect_tx(bar, __popc(vm) * 2 * H::kChunks * p.R * 128 + (first ? gc * D * 2 : 0));
     }
     __syncwarp();
     if (valid) {
-      const uint32_t hs = p.R * 128;              // one half of one box
-      const uint32_t dk = sk + lane * 2 * hs;     // this lane's box
+      const uint32_t hs = p.R * 128;                     // one chunk of one box
+      const uint32_t dk = sk + lane * H::kChunks * hs;   // this lane's box
       if (p.map5d) {
         tma_load_5d(dk, &tmK, 0, pslot, 0, ic.kvh, phys, bar);
         tma_load_5d(dk + C::kKV, &tmV, 0, pslot, 0, ic.kvh, phys, bar);
       } else {
-        tma_load_4d(dk, &tmK, 0, ic.kvh, pslot, phys, bar);
-        tma_load_4d(dk + hs, &tmK, 64, ic.kvh, pslot, phys, bar);
-        tma_load_4d(dk + C::kKV, &tmV, 0, ic.kvh, pslot, phys, bar);
-        tma_load_4d(dk + C::kKV + hs, &tmV, 64, ic.kvh, pslot, phys, bar);
+#pragma unroll
+        for (int c = 0; c < H::kChunks; ++c) {
+          tma_load_4d(dk + c * hs, &tmK, 64 * c, ic.kvh, pslot, phys, bar);
+          tma_load_4d(dk + C::kKV + c * hs, &tmV, 64 * c, ic.kvh, pslot, phys, bar);
+        }
       }
     }
     if (first && lane < gc) {
       const int hq = ic.kvh * G + ic.qc * 8 + lane;
-      bulk_load(sk + 2 * C::kKV + lane * kD * 2, p.q + ic.b * p.q_sb + hq * p.q_sh, kD * 2, bar);
+      bulk_load(sk + 2 * C::kKV + lane * D * 2, p.q + ic.b * p.q_sb + hq * p.q_sh, D * 2, bar);
     }
     ++issued;
     // advance to the next tile
@@ -864,8 +928,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---- consumer state
-  uint32_t qf[8][2];
-  float acc[8][4];
+  uint32_t qf[H::kSteps][2];
+  float acc[H::kSteps][4];
   float m_run[2], l_run[2];
   uint32_t phase = 0;
   uint32_t mask_hi = 0, mask_lo = 0;   // which 16-bit halves carry hi / lo of p
@@ -874,8 +938,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
   const float scl = p.scale_log2;
 
   // ldmatrix lane offsets in the box-major, 128-byte-swizzled tile: token row r
-  // sits at r*128 + (r/R)*R*128 (box start plus the other half of earlier
-  // boxes), 16-byte chunk c of a half at ((c ^ (r & 7)) << 4), half 1 at +R*128.
+  // sits at r*128 + (r/R)*R*128*(D/64 - 1) (box start plus the other chunks of
+  // earlier boxes), 16-byte piece c of a chunk at ((c ^ (r & 7)) << 4), chunk q
+  // at +q*R*128.
   const uint32_t hs = p.R * 128;
   uint32_t offk[kMB], offv[kMB], swzk[4], swzv[4];
   {
@@ -885,8 +950,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
 #pragma unroll
     for (int mb = 0; mb < kMB; ++mb) {
       const int r1 = mb * 16 + rk, r2 = mb * 16 + rv;
-      offk[mb] = r1 * 128 + ((r1 >> p.lR) << p.lR) * 128;
-      offv[mb] = r2 * 128 + ((r2 >> p.lR) << p.lR) * 128;
+      offk[mb] = r1 * 128 + ((r1 >> p.lR) << p.lR) * 128 * (H::kChunks - 1);
+      offv[mb] = r2 * 128 + ((r2 >> p.lR) << p.lR) * 128 * (H::kChunks - 1);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -922,19 +987,19 @@ __global__ void __launch_bounds__(NW * 32, 1)
       const int n = rr;
       const int head = kDup ? (n < 2 * gc ? (n < gc ? n : n - gc) : -1) : (n < gc ? n : -1);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+      for (int ks = 0; ks < H::kSteps; ++ks) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t v = 0;
           if (head >= 0) {
-            const uint32_t addr = sq + head * kD * 2 + (ks * 16 + h * 8 + qd * 2) * 2;
+            const uint32_t addr = sq + head * D * 2 + (ks * 16 + h * 8 + qd * 2) * 2;
             asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
           }
           qf[ks][h] = v;
         }
       }
 #pragma unroll
-      for (int md = 0; md < 8; ++md)
+      for (int md = 0; md < H::kSteps; ++md)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[md][r] = 0.f;
       m_run[0] = m_run[1] = -INFINITY;
@@ -956,7 +1021,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 #pragma unroll
       for (int r = 0; r < 4; ++r) s[mb][r] = 0.f;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+      for (int ks = 0; ks < H::kSteps; ++ks) {
         uint32_t a[4];
         ldsm_x4(sk + offk[mb] + (ks >> 2) * hs + swzk[ks & 3], a);
         Mma<T>::run(s[mb], a, qf[ks][0], qf[ks][1]);
@@ -1002,7 +1067,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     l_run[1] = fmaf(l_run[1], alpha[1], psum[1]);
     if (__any_sync(kFull, (alpha[0] != 1.f) || (alpha[1] != 1.f))) {
 #pragma unroll
-      for (int md = 0; md < 8; ++md) {
+      for (int md = 0; md < H::kSteps; ++md) {
         acc[md][0] *= alpha[0];
         acc[md][1] *= alpha[1];
         acc[md][2] *= alpha[0];
@@ -1039,7 +1104,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
               ((tk + 9 >= t0 && tk + 9 < t1) ? 0xffff0000u : 0u);
       }
 #pragma unroll
-      for (int md = 0; md < 8; ++md) {
+      for (int md = 0; md < H::kSteps; ++md) {
         uint32_t a[4];
         ldsm_x4_t(sv + offv[kb] + (md >> 2) * hs + swzv[md & 3], a);
         if (partial) {
@@ -1073,9 +1138,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
       lsum[e] = v;
     }
     // Dup layout: column c + gc holds the low part of column c.
-    float o[8][4];
+    float o[H::kSteps][4];
 #pragma unroll
-    for (int md = 0; md < 8; ++md)
+    for (int md = 0; md < H::kSteps; ++md)
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         float v = acc[md][r];
@@ -1104,7 +1169,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (dest == 0) {
         char* dst = p.out + b * p.o_sb + hq * p.o_sh;
 #pragma unroll
-        for (int md = 0; md < 8; ++md) {
+        for (int md = 0; md < H::kSteps; ++md) {
           const int d0i = md * 16 + rr;
           *reinterpret_cast<uint16_t*>(dst + d0i * 2) = Mma<T>::from_float(o[md][e] * inv_l);
           *reinterpret_cast<uint16_t*>(dst + (d0i + 8) * 2) =
@@ -1115,18 +1180,18 @@ __global__ void __launch_bounds__(NW * 32, 1)
         float* od;
         float* ld;
         if (dest == 2) {
-          od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * kSlotStride;
-          ld = od + kD;
+          od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * H::kSlotStride;
+          ld = od + D;
         } else if (p.ns == 0) {
-          od = gslot_row(p, gslot, c);
+          od = gslot_row<D>(p, gslot, c);
           ld = gslot_lse(p, gslot, c);
         } else {
           const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + w.s;
-          od = p.o_part + row * kD;
+          od = p.o_part + row * D;
           ld = p.lse_part + row;
         }
 #pragma unroll
-        for (int md = 0; md < 8; ++md) {
+        for (int md = 0; md < H::kSteps; ++md) {
           const int d0i = md * 16 + rr;
           od[d0i] = o[md][e] * inv_l;
           od[d0i + 8] = o[md][e + 2] * inv_l;
@@ -1146,12 +1211,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
       last = __shfl_sync(kFull, last, 0);
       if (!last) continue;
       __threadfence();
-      merge_splits<T>(p, b, kvh, qc, gc, lane);
+      merge_splits<T, D>(p, b, kvh, qc, gc, lane);
       if (lane == 0) atomicExch(p.counters + cid, 0);
       continue;
     }
     if (dest == 1) {
-      publish_group<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+      publish_group<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
       continue;
     }
 
@@ -1172,20 +1237,20 @@ __global__ void __launch_bounds__(NW * 32, 1)
         const int wk = w_first + k;
         const int start = rg.gr0 + wk * rg.Pw;
         const int side = (max(glo, start) == start) ? 0 : 1;
-        row = gslots + ((wk * 2 + side) * p.slot_cols + j) * kSlotStride;
-        lp = row + kD;
+        row = gslots + ((wk * 2 + side) * p.slot_cols + j) * H::kSlotStride;
+        lp = row + D;
       };
-      float4 o4;
+      RowV<H::kLaneF> o4;
       float lse;
-      merge_rows<false>(nw, lane, src, o4, lse);
+      merge_rows<false, D>(nw, lane, src, o4, lse);
       if (fl & kGroupSeg) {
-        store_out4<T>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
+        store_out<T, D>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
       } else {
-        *(reinterpret_cast<float4*>(gslot_row(p, gslot, j)) + lane) = o4;
+        store_row(gslot_row<D>(p, gslot, j), lane, o4);
         if (lane == 0) *gslot_lse(p, gslot, j) = lse;
       }
     }
-    if (!(fl & kGroupSeg)) publish_group<T>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+    if (!(fl & kGroupSeg)) publish_group<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
   }
 }
 
@@ -1332,11 +1397,13 @@ struct Variant {
   int tile, nw, ns;
 };
 static const Variant kVariants[] = {
-    {32, 4, 3},   // 1
-    {16, 8, 3},   // 2 (dup layout only: 9 KB stages)
-    {32, 6, 2},   // 3
-    {16, 12, 2},  // 4 (dup layout only)
-    {16, 8, 2},   // 5
+    {32, 4, 3},   // 1 (head_dim 128)
+    {16, 8, 3},   // 2 (head_dim 128, dup layout only: 9 KB stages)
+    {32, 6, 2},   // 3 (head_dim 64 or 128)
+    {16, 12, 2},  // 4 (head_dim 128, dup layout only)
+    {16, 8, 2},   // 5 (head_dim 64 or 128)
+    {16, 4, 2},   // 6 (head_dim 256: 16 KB K+V tiles)
+    {16, 5, 2},   // 7 (head_dim 256)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // Opt-in shared memory per CTA is 227 KB (232448 B), static plus dynamic; the
@@ -1348,6 +1415,7 @@ struct Plan {
   int grid = 0;
   int W = 0;
   int G = 1, QC = 1;
+  int D = 128;       // head_dim
   bool dup = true;
   int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
@@ -1359,18 +1427,36 @@ struct Plan {
 };
 
 // Shared memory a variant needs before the group merge area.
-template <bool kDup, int TILE, int NW, int NS>
+template <bool kDup, int TILE, int NW, int NS, int D>
 static int smem_base() {
-  return Cfg<kDup, TILE, NW, NS>::kSmemBase;
+  return Cfg<kDup, TILE, NW, NS, D>::kSmemBase;
 }
 
-static int variant_smem_base(int variant, bool dup) {
+// Whether (head_dim, variant, layout) is instantiated.
+static bool variant_built(int D, int variant, bool dup) {
+  switch (D) {
+    case 64: return variant == 3 || variant == 5;
+    case 128: return variant >= 1 && variant <= 5 && (dup || (variant != 2 && variant != 4));
+    case 256: return variant == 6 || variant == 7;
+    default: return false;
+  }
+}
+
+static int variant_smem_base(int variant, bool dup, int D) {
+  if (D == 64) {
+    if (variant == 3) return dup ? smem_base<true, 32, 6, 2, 64>() : smem_base<false, 32, 6, 2, 64>();
+    return dup ? smem_base<true, 16, 8, 2, 64>() : smem_base<false, 16, 8, 2, 64>();
+  }
+  if (D == 256) {
+    if (variant == 7) return dup ? smem_base<true, 16, 5, 2, 256>() : smem_base<false, 16, 5, 2, 256>();
+    return dup ? smem_base<true, 16, 4, 2, 256>() : smem_base<false, 16, 4, 2, 256>();
+  }
   switch (variant) {
-    case 2: return dup ? smem_base<true, 16, 8, 3>() : 0;
-    case 3: return dup ? smem_base<true, 32, 6, 2>() : smem_base<false, 32, 6, 2>();
-    case 4: return dup ? smem_base<true, 16, 12, 2>() : 0;
-    case 5: return dup ? smem_base<true, 16, 8, 2>() : smem_base<false, 16, 8, 2>();
-    default: return dup ? smem_base<true, 32, 4, 3>() : smem_base<false, 32, 4, 3>();
+    case 2: return dup ? smem_base<true, 16, 8, 3, 128>() : 0;
+    case 3: return dup ? smem_base<true, 32, 6, 2, 128>() : smem_base<false, 32, 6, 2, 128>();
+    case 4: return dup ? smem_base<true, 16, 12, 2, 128>() : 0;
+    case 5: return dup ? smem_base<true, 16, 8, 2, 128>() : smem_base<false, 16, 8, 2, 128>();
+    default: return dup ? smem_base<true, 32, 4, 3, 128>() : smem_base<false, 32, 4, 3, 128>();
   }
 }
 
@@ -1388,30 +1474,47 @@ static pa_status_t validate(const pa_decode_params* p) {
                                     static_cast<long long>(p->max_blocks) * p->block_size)
     return PA_ERR_ARG;
   if (p->kernel_variant < 0 || p->kernel_variant > kNumVariants) return PA_ERR_ARG;
-  if (p->head_dim != kD) return PA_ERR_UNSUPPORTED;
+  if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) return PA_ERR_UNSUPPORTED;
+  if (p->kernel_variant != 0) {   // an explicit variant must be built for this head_dim
+    const int g = p->num_heads / p->num_kv_heads;
+    const bool dup = (g == 1 || g == 2 || g == 4);
+    int v = p->kernel_variant;
+    if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
+    if (!variant_built(p->head_dim, v, dup)) return PA_ERR_UNSUPPORTED;
+  }
   if (p->block_size % 8 != 0 || p->block_size > (1 << 20)) return PA_ERR_UNSUPPORTED;
   return PA_OK;
 }
 
-// Automatic choice, from B200 sweeps of the five benchmark shapes: MHA with
-// pages shorter than 32 tokens, and groups larger than 4 query heads, stream
-// best as 16-token tiles on 8 warps; longer pages and 2- or 4-head groups as
-// 32-token tiles on 6 warps.
+// Automatic choice, from B200 sweeps. head_dim 128 (the five benchmark
+// shapes): MHA with pages shorter than 32 tokens, and groups larger than 4
+// query heads, stream best as 16-token tiles on 8 warps; longer pages and 2- or
+// 4-head groups as 32-token tiles on 6 warps. head_dim 64: 32-token tiles on 6
+// warps throughout. head_dim 256: 16-token tiles on 5 warps, or 4 warps when
+// the query columns cannot be duplicated (the merge area of 5 warps x 8
+// columns does not fit).
 static int pick_variant(const pa_decode_params* p, bool dup) {
   int v = p->kernel_variant;
   if (v == 0) {
     const int g = p->num_heads / p->num_kv_heads;
-    v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
+    if (p->head_dim == 256)
+      v = dup ? 7 : 6;      // 5 warps where their merge area fits (up to 4 query columns)
+    else if (p->head_dim == 64)
+      v = 3;                // 32-token tiles of 128-byte rows
+    else
+      v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
   }
-  if (!dup && (v == 2 || v == 4)) v = 5;
-  return v;
+  if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
+  return variant_built(p->head_dim, v, dup) ? v : 0;   // 0: not built for this head_dim
 }
 
 static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
   pl.G = p->num_heads / p->num_kv_heads;
   pl.QC = (pl.G + 7) / 8;
   pl.dup = (pl.G == 1 || pl.G == 2 || pl.G == 4);
+  pl.D = p->head_dim;
   pl.variant = pick_variant(p, pl.dup);
+  if (pl.variant == 0) return PA_ERR_UNSUPPORTED;
   const Variant& v = kVariants[pl.variant - 1];
   const long long nseg = static_cast<long long>(p->num_kv_heads) * pl.QC;
   const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
@@ -1432,30 +1535,30 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     pl.W = pl.grid * v.nw;
     pl.use_cum = p->seq_lens != nullptr;
     // Merge pieces inside a CTA through shared memory when the warps' rows fit.
-    const int base = variant_smem_base(pl.variant, pl.dup);
-    const int group_bytes = v.nw * 2 * kSlotStride * 4 * pl.slot_cols;
+    const int base = variant_smem_base(pl.variant, pl.dup, pl.D);
+    const int group_bytes = v.nw * 2 * (pl.D + 4) * 4 * pl.slot_cols;
     pl.gsz = (base + group_bytes <= kMaxSmem) ? v.nw : 1;
     pl.smem = base + (pl.gsz > 1 ? group_bytes : 0);
     const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);   // two per group
-    pl.ws_bytes = slots * pl.slot_cols * (kD + 1) * sizeof(float);
+    pl.ws_bytes = slots * pl.slot_cols * (pl.D + 1) * sizeof(float);
   } else {
-    pl.smem = variant_smem_base(pl.variant, pl.dup);
+    pl.smem = variant_smem_base(pl.variant, pl.dup, pl.D);
     const long long workers = static_cast<long long>(p->batch) * nseg * pl.ns;
     if (workers > 0x7fffffffll) return PA_ERR_UNSUPPORTED;
     pl.W = static_cast<int>(workers);
     pl.grid = static_cast<int>((workers + v.nw - 1) / v.nw);
     const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
-    pl.ws_bytes = (p->o_partial && p->lse_partial) ? 0 : rows * (kD + 1) * sizeof(float);
+    pl.ws_bytes = (p->o_partial && p->lse_partial) ? 0 : rows * (pl.D + 1) * sizeof(float);
   }
   pl.counters = static_cast<size_t>(p->batch) * nseg;
   return PA_OK;
 }
 
-// Tensor map of one paged cache [num_blocks, block_size, Hkv, 128]. The 5-D
-// form orders the dimensions (64 dims, slot, dim-half, head, block) so that one
-// box of {64, R, 2, 1, 1} lands as [half][R rows][128 B]: both halves of R token
-// rows in one copy. The 4-D form {128 dims, head, slot, block} with box
-// {64, 1, R, 1} needs one copy per half.
+// Tensor map of one paged cache [num_blocks, block_size, Hkv, D]. The 5-D form
+// orders the dimensions (64 dims, slot, 64-dim chunk, head, block) so that one
+// box of {64, R, D/64, 1, 1} lands as [chunk][R rows][128 B]: all chunks of R
+// token rows in one copy. The 4-D form {D dims, head, slot, block} with box
+// {64, 1, R, 1} needs one copy per chunk.
 static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const void* base,
                              int64_t s_block, int64_t s_slot, int64_t s_head, int rows,
                              bool five_d) {
@@ -1465,19 +1568,22 @@ static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const 
       p->dtype == PA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r;
   if (five_d) {
-    cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(p->block_size), 2,
+    cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(p->block_size),
+                          static_cast<cuuint64_t>(p->head_dim / 64),
                           static_cast<cuuint64_t>(p->num_kv_heads),
                           static_cast<cuuint64_t>(p->num_blocks)};
     cuuint64_t strides[4] = {static_cast<cuuint64_t>(s_slot) * 2, 128,
                              static_cast<cuuint64_t>(s_head) * 2,
                              static_cast<cuuint64_t>(s_block) * 2};
-    cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows), 2, 1, 1};
+    cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows),
+                         static_cast<cuuint32_t>(p->head_dim / 64), 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     r = fn(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
-    cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(p->num_kv_heads),
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(p->head_dim),
+                          static_cast<cuuint64_t>(p->num_kv_heads),
                           static_cast<cuuint64_t>(p->block_size),
                           static_cast<cuuint64_t>(p->num_blocks)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2,
@@ -1496,12 +1602,13 @@ static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const 
 // K/V cache pointers every step. Small round-robin cache, keyed by everything
 // the encoding depends on.
 struct MapKey {
-  int dev, dtype, rows, five_d;
+  int dev, dtype, rows, five_d, head_dim;
   const void* base;
   int64_t dims[3];      // block_size, num_kv_heads, num_blocks
   int64_t strides[3];   // block, slot, head (elements)
   bool operator==(const MapKey& o) const {
     return dev == o.dev && dtype == o.dtype && rows == o.rows && five_d == o.five_d &&
+           head_dim == o.head_dim &&
            base == o.base && memcmp(dims, o.dims, sizeof(dims)) == 0 &&
            memcmp(strides, o.strides, sizeof(strides)) == 0;
   }
@@ -1521,6 +1628,7 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
   key.dtype = p->dtype;
   key.rows = rows;
   key.five_d = five_d ? 1 : 0;
+  key.head_dim = p->head_dim;
   key.base = base;
   key.dims[0] = p->block_size;
   key.dims[1] = p->num_kv_heads;
@@ -1548,16 +1656,16 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
-template <typename T, bool kDup, int TILE, int NW, int NS>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D>
 static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                               const KParams& kp, cudaStream_t stream, int dev) {
-  using C = Cfg<kDup, TILE, NW, NS>;
+  using C = Cfg<kDup, TILE, NW, NS, D>;
   static_assert(C::kSmemBase <= kMaxSmem, "shared memory plan exceeds 227 KB");
   static bool attr_set[64] = {false};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS>,
+      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kMaxSmem);
       if (e != cudaSuccess) return e;
@@ -1577,27 +1685,35 @@ static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUten
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS>, mk, mv, kp);
+  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D>, mk, mv, kp);
 }
 
 template <typename T, bool kDup>
 static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                           const KParams& kp, cudaStream_t stream, int dev) {
+  if (pl.D == 64) {
+    if (pl.variant == 3) return launch_one<T, kDup, 32, 6, 2, 64>(pl, mk, mv, kp, stream, dev);
+    return launch_one<T, kDup, 16, 8, 2, 64>(pl, mk, mv, kp, stream, dev);
+  }
+  if (pl.D == 256) {
+    if (pl.variant == 7) return launch_one<T, kDup, 16, 5, 2, 256>(pl, mk, mv, kp, stream, dev);
+    return launch_one<T, kDup, 16, 4, 2, 256>(pl, mk, mv, kp, stream, dev);
+  }
   switch (pl.variant) {
     case 2:
-      if constexpr (kDup) return launch_one<T, kDup, 16, 8, 3>(pl, mk, mv, kp, stream, dev);
+      if constexpr (kDup) return launch_one<T, kDup, 16, 8, 3, 128>(pl, mk, mv, kp, stream, dev);
       break;
     case 3:
-      return launch_one<T, kDup, 32, 6, 2>(pl, mk, mv, kp, stream, dev);
+      return launch_one<T, kDup, 32, 6, 2, 128>(pl, mk, mv, kp, stream, dev);
     case 4:
-      if constexpr (kDup) return launch_one<T, kDup, 16, 12, 2>(pl, mk, mv, kp, stream, dev);
+      if constexpr (kDup) return launch_one<T, kDup, 16, 12, 2, 128>(pl, mk, mv, kp, stream, dev);
       break;
     case 5:
-      return launch_one<T, kDup, 16, 8, 2>(pl, mk, mv, kp, stream, dev);
+      return launch_one<T, kDup, 16, 8, 2, 128>(pl, mk, mv, kp, stream, dev);
     default:
       break;
   }
-  return launch_one<T, kDup, 32, 4, 3>(pl, mk, mv, kp, stream, dev);
+  return launch_one<T, kDup, 32, 4, 3, 128>(pl, mk, mv, kp, stream, dev);
 }
 
 }  // namespace pa
@@ -1693,7 +1809,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   if (pl.ns == 0) {
     float* ws = static_cast<float*>(p->workspace);
     kp.o_part = ws;
-    kp.lse_part = ws + static_cast<size_t>(2) * (pl.W / pl.gsz) * pl.slot_cols * kD;
+    kp.lse_part = ws + static_cast<size_t>(2) * (pl.W / pl.gsz) * pl.slot_cols * pl.D;
   } else if (p->o_partial && p->lse_partial) {
     kp.o_part = p->o_partial;
     kp.lse_part = p->lse_partial;
@@ -1701,7 +1817,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
     float* ws = static_cast<float*>(p->workspace);
     const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
     kp.o_part = ws;
-    kp.lse_part = ws + rows * kD;
+    kp.lse_part = ws + rows * pl.D;
   }
   kp.counters = p->counters;
   kp.status = p->status;

@@ -41,7 +41,7 @@ from . import _native
 from ._native import DecodeParams, PagedAttentionError
 from .split_kv_kernel import LSE_SENTINEL  # noqa: F401  (re-exported constant)
 
-HEAD_DIM = 128
+HEAD_DIMS = (64, 128, 256)   # head dimensions the kernel is built for
 
 _DTYPES = {torch.float16: _native.PA_F16, torch.bfloat16: _native.PA_BF16}
 

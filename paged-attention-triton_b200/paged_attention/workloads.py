@@ -62,12 +62,13 @@ class Workload:
     def effective_bytes(self) -> int:
         """``sum_b S_b * Hkv * D * e * 2 + B * Hq * D * e * 2`` (K+V, then q+o)."""
         e = self.q.element_size()
-        kv = sum(self.seq_list()) * self.num_kv_heads * HEAD_DIM * e * 2
-        return kv + self.batch * self.num_heads * HEAD_DIM * e * 2
+        d = self.q.shape[-1]
+        kv = sum(self.seq_list()) * self.num_kv_heads * d * e * 2
+        return kv + self.batch * self.num_heads * d * e * 2
 
     def flops(self) -> int:
         """``4 * sum_b S_b * Hq * D`` (q.k and p.v multiply-adds)."""
-        return 4 * sum(self.seq_list()) * self.num_heads * HEAD_DIM
+        return 4 * sum(self.seq_list()) * self.num_heads * self.q.shape[-1]
 
 
 def _gen(seed: int, device) -> torch.Generator:
@@ -82,13 +83,13 @@ def _randn(shape, g, device, dtype):
 
 def build(name: str, b: int, hq: int, hkv: int, bs: int, dtype: torch.dtype,
           seq_lens: Union[int, torch.Tensor], max_blocks: int, pool: int, seed: int,
-          device="cuda") -> Workload:
+          device="cuda", head_dim: int = HEAD_DIM) -> Workload:
     """Generic builder: shuffled pool, every row's blocks distinct."""
     device = torch.device(device)
     g = _gen(seed, device)
-    q = _randn((b, hq, HEAD_DIM), g, device, dtype)
-    k = _randn((pool, bs, hkv, HEAD_DIM), g, device, dtype)
-    v = _randn((pool, bs, hkv, HEAD_DIM), g, device, dtype)
+    q = _randn((b, hq, head_dim), g, device, dtype)
+    k = _randn((pool, bs, hkv, head_dim), g, device, dtype)
+    v = _randn((pool, bs, hkv, head_dim), g, device, dtype)
     need = b * max_blocks
     if need <= pool:
         perm = torch.randperm(pool, generator=g, device=device)[:need]

@@ -32,7 +32,7 @@ import torch  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 
-# name, seed, dtype, B, H, S, block_size, pool blocks, num_splits, table
+# name, seed, dtype, B, H, S, block_size, pool blocks, num_splits, table[, head_dim]
 CASES = [
     ("mha_f16_b2_s100_bs16_ns3", 1, "float16", 2, 2, 100, 16, 16, 3, "shuffle"),
     ("mha_f16_s9_bs16_ns4_empty_split", 2, "float16", 1, 2, 9, 16, 4, 4, "shuffle"),
@@ -44,6 +44,11 @@ CASES = [
     # tests/correctness.py:9-36 style: seed 42, identity block table, heuristic
     # num_splits for a 148-SM part (min(ceil(256/16), 148*4 // (1*4)) = 16).
     ("correctness_f16_b1_h4_s256_bs16_identity", 42, "float16", 1, 4, 256, 16, 16, 16, "identity"),
+    # head dimensions other than 128 (the reference kernel takes D as a constexpr)
+    ("mha_f16_d64_b2_s100_bs16_ns3", 11, "float16", 2, 2, 100, 16, 16, 3, "shuffle", 64),
+    ("mha_bf16_d64_s9_bs8_ns4_empty_split", 12, "bfloat16", 1, 2, 9, 8, 4, 4, "shuffle", 64),
+    ("mha_f16_d256_s130_bs16_ns3", 13, "float16", 1, 2, 130, 16, 12, 3, "shuffle", 256),
+    ("mha_bf16_d256_b2_s40_bs32_ns2", 14, "bfloat16", 2, 1, 40, 32, 6, 2, "shuffle", 256),
 ]
 
 
@@ -53,13 +58,12 @@ def _bits(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().numpy()
 
 
-def make_case(ref_pkg, name, seed, dtype_name, b, h, s, bs, pool, ns, table):
+def make_case(ref_pkg, name, seed, dtype_name, b, h, s, bs, pool, ns, table, d=128):
     from paged_attention import paged_attention  # reference package
     from paged_attention.split_kv_kernel import (
         paged_attention_split_kernel, LSE_SENTINEL)
 
     dtype = getattr(torch, dtype_name)
-    d = 128
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(b, h, d, generator=g).to(dtype)
     k = torch.randn(pool, bs, h, d, generator=g).to(dtype)
@@ -76,7 +80,8 @@ def make_case(ref_pkg, name, seed, dtype_name, b, h, s, bs, pool, ns, table):
     o_ref = paged_attention(q, k, v, bt, s, bs, ns)
 
     split_size = (s + ns - 1) // ns
-    o_part = torch.empty(b, h, ns, d, dtype=torch.float16)
+    # zero-filled so the rows of empty splits (never written) are reproducible
+    o_part = torch.zeros(b, h, ns, d, dtype=torch.float16)
     lse_part = torch.empty(b, h, ns, dtype=torch.float32)
     lse_part.fill_(LSE_SENTINEL)
     paged_attention_split_kernel[(b * h, ns)](

@@ -91,7 +91,12 @@ def _params(**kw):
     ({"dtype": 7}, _native.PA_ERR_ARG),
     ({"seq_len": 65}, _native.PA_ERR_ARG),                          # > max_blocks * bs
     ({"num_splits": -1}, _native.PA_ERR_ARG),
-    ({"head_dim": 64}, _native.PA_ERR_UNSUPPORTED),
+    ({"head_dim": 96}, _native.PA_ERR_UNSUPPORTED),
+    ({"head_dim": 32}, _native.PA_ERR_UNSUPPORTED),
+    ({"head_dim": 256, "kernel_variant": 3}, _native.PA_ERR_UNSUPPORTED),   # not built for 256
+    ({"head_dim": 64, "kernel_variant": 1}, _native.PA_ERR_UNSUPPORTED),    # not built for 64
+    ({"head_dim": 128, "kernel_variant": 6}, _native.PA_ERR_UNSUPPORTED),   # not built for 128
+    ({"kernel_variant": 8}, _native.PA_ERR_ARG),                            # no such variant
     ({"block_size": 12, "seq_len": 40}, _native.PA_ERR_UNSUPPORTED),
 ])
 def test_host_validation_without_gpu(kw, code):
@@ -100,6 +105,18 @@ def test_host_validation_without_gpu(kw, code):
     a, b = ctypes.c_size_t(0), ctypes.c_size_t(0)
     assert lib.pa_decode_workspace(ctypes.byref(p), ctypes.byref(a), ctypes.byref(b)) == code
     assert lib.pa_decode(ctypes.byref(p), None) == code
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
+def test_workspace_scales_with_head_dim(head_dim):
+    """Split-schedule partials are [B, Hq, ns, D] floats plus one LSE each."""
+    lib = _native.lib()
+    p = _params(head_dim=head_dim, num_splits=3)
+    a, b = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    assert lib.pa_decode_workspace(ctypes.byref(p), ctypes.byref(a), ctypes.byref(b)) == 0
+    assert a.value == 2 * 8 * 3 * (head_dim + 1) * 4
+    assert b.value == 2 * 2          # one counter per (row, KV head)
 
 
 def test_null_params_rejected():
