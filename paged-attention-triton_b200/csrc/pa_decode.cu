@@ -404,7 +404,7 @@ __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
 // serves box (L & (spt-1)) of tile (L >> lspt) of the batch [u0, u1) (units of
 // the warp range, or tile ordinals of a split). INT_MIN: the box holds no token
 // of its piece (not loaded; the consumer masks it). One load per lane.
-template <int TILE>
+template <int TILE, bool kSplit>
 __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, const Ranges& rg,
                                             const Work& w, int u0, int u1, int lane, int& phys,
                                             int& slot) {
@@ -414,7 +414,7 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
   slot = 0;
   if (u0 + ord < u1) {
     int tile, b, t0, t1;
-    if (p.ns == 0) {
+    if constexpr (!kSplit) {
       Cursor c;
       decode_unit<TILE>(c, p, cum, u0 + ord);
       int fl;
@@ -666,7 +666,7 @@ __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
-template <typename T, bool kDup, int TILE, int NW, int NS, int D>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit>
 __global__ void __launch_bounds__(NW * 32, 1)
     pa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const KParams p) {
@@ -717,7 +717,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
   };
   // Same-length rows: the ranges need no memory, so they are set before the wait.
-  if (p.ns == 0 && !p.use_cum) set_ranges(p.U, p.P, p.Pw);
+  if (!kSplit && !p.use_cum) set_ranges(p.U, p.P, p.Pw);
 
   // Programmatic dependent launch: everything above touches no global memory;
   // from here on the kernel reads inputs (and writes outputs, partials and
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
-  if (p.ns == 0 && p.use_cum) {
+  if (!kSplit && p.use_cum) {
     const int B = p.B;
     const int nseg = p.Hkv * p.QC;
     const int chunk = (B + blockDim.x - 1) / blockDim.x;
@@ -759,7 +759,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
 
   // Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
-  if (p.ns == 0 && p.zero_rows) {
+  if (!kSplit && p.zero_rows) {
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (row_len(p, b) != 0) continue;
       for (int idx = threadIdx.x; idx < p.Hq * (D / 8); idx += blockDim.x) {
@@ -778,7 +778,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   Work w;
   w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
   int n_tiles = 0;
-  if (p.ns == 0) {
+  if (!kSplit) {
     if (p.use_cum) {
       const int U = cum[p.B];
       const int P = max(static_cast<int>(fast_div(static_cast<uint32_t>(U) + p.div_ng.d - 1,
@@ -807,8 +807,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     n_tiles = w.n;
   }
   // range of this warp's units (balanced) or of its split's tile ordinals
-  const int range0 = (p.ns == 0) ? rg.wr0 : 0;
-  const int range1 = (p.ns == 0) ? rg.wr1 : w.n;
+  const int range0 = (!kSplit) ? rg.wr0 : 0;
+  const int range1 = (!kSplit) ? rg.wr1 : w.n;
 
   const uint32_t stage0 = smem_u32(smem + warp * NS * C::kStage);
   const uint32_t bar0 = smem_u32(&bars[warp * NS]);
@@ -816,7 +816,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
   // Split schedule, empty split (split_kv_kernel.py:32-33): the partial LSE keeps
   // the sentinel; the last arriving split of the segment merges.
-  if (p.ns != 0 && w.n == 0) {
+  if (kSplit && w.n == 0) {
     const int gc = min(8, G - w.qc * 8);
     for (int j = 0; j < gc; ++j) {
       const int hq = w.kvh * G + w.qc * 8 + j;
@@ -841,20 +841,20 @@ __global__ void __launch_bounds__(NW * 32, 1)
   int u0c = range0, u1c = min(range1, range0 + bt_tiles);
   int u0n = u1c, u1n = min(range1, u1c + bt_tiles);
   int pg_c = INT_MIN, sl_c = 0, pg_n = INT_MIN, sl_n = 0;
-  if (u0c < u1c) batch_pages<TILE>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
+  if (u0c < u1c) batch_pages<TILE, kSplit>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
   Cursor ic;
   ic.b = w.b;
   ic.kvh = w.kvh;
   ic.qc = w.qc;
   ic.tile = w.tl0;
   ic.nt = ic.S = ic.seg_lo = 0;
-  if (p.ns == 0 && n_tiles > 0) decode_unit<TILE>(ic, p, cum, range0);
+  if (!kSplit && n_tiles > 0) decode_unit<TILE>(ic, p, cum, range0);
   int ord = 0;          // tile ordinal within the current batch
   int issued = 0;
 
   auto issue = [&](int st) {
     int t0, t1, fl;
-    if (p.ns == 0) {
+    if (!kSplit) {
       piece_of<TILE>(ic, rg, t0, t1, fl);
     } else {
       const int k = u0c + ord;
@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     ++issued;
     // advance to the next tile
-    if (p.ns == 0) cursor_next<TILE>(ic, p); else ++ic.tile;
+    if (!kSplit) cursor_next<TILE>(ic, p); else ++ic.tile;
     if (u0c + ++ord < u1c) return;
     u0c = u0n;
     u1c = u1n;
@@ -913,7 +913,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     ord = 0;
     u0n = u1c;
     u1n = min(range1, u1c + bt_tiles);
-    if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
+    if (u0n < u1n) batch_pages<TILE, kSplit>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   };
 
   for (int s = 0; s < NS && issued < n_tiles; ++s) issue(s);
@@ -921,8 +921,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // batch holds at least 8 tiles (32 boxes of >= 8 rows), more than the NS
   // issued above, so those never reached it (a range that ended inside the
   // first batch has no second one).
-  if (u0n < u1n) batch_pages<TILE>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
-  if (p.ns == 0) __syncthreads();   // gcnt is zero for every warp's merges
+  if (u0n < u1n) batch_pages<TILE, kSplit>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
+  if (!kSplit) __syncthreads();   // gcnt is zero for every warp's merges
   // The next kernel in the stream may start its own prologue on SMs this grid
   // leaves; it waits for this grid's completion before touching memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1154,7 +1154,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
     // Where this warp's piece goes: 0 final output, 1 the group's global slot
     // (or the split's row), 2 this warp's shared-memory slot.
-    const int dest = (p.ns != 0) ? 1 : (fl & kWarpSeg) ? 0 : (fl & kWarpGroup) ? 1 : 2;
+    const int dest = (kSplit) ? 1 : (fl & kWarpSeg) ? 0 : (fl & kWarpGroup) ? 1 : 2;
     const int glo = max(seg_lo, rg.gr0), ghi = min(seg_hi, rg.gr1);
     const long long gslot = 2ll * rg.g + (glo == rg.gr0 ? 0 : 1);
     const int wside = (max(seg_lo, rg.wr0) == rg.wr0) ? 0 : 1;
@@ -1182,7 +1182,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
         if (dest == 2) {
           od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * H::kSlotStride;
           ld = od + D;
-        } else if (p.ns == 0) {
+        } else if (!kSplit) {
           od = gslot_row<D>(p, gslot, c);
           ld = gslot_lse(p, gslot, c);
         } else {
@@ -1201,7 +1201,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     if (dest == 0) continue;
 
-    if (p.ns != 0) {
+    if (kSplit) {
       // split schedule: the last split of the segment merges all ns rows
       __threadfence();
       __syncwarp();
@@ -1656,16 +1656,16 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
-template <typename T, bool kDup, int TILE, int NW, int NS, int D>
-static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
-                              const KParams& kp, cudaStream_t stream, int dev) {
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit>
+static cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
+                                 const KParams& kp, cudaStream_t stream, int dev) {
   using C = Cfg<kDup, TILE, NW, NS, D>;
   static_assert(C::kSmemBase <= kMaxSmem, "shared memory plan exceeds 227 KB");
   static bool attr_set[64] = {false};
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D>,
+      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kMaxSmem);
       if (e != cudaSuccess) return e;
@@ -1685,7 +1685,16 @@ static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUten
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D>, mk, mv, kp);
+  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>, mk, mv, kp);
+}
+
+// The balanced and the split schedule are separate kernels: neither carries
+// the other's code (the kernels are bound by instruction fetch on short steps).
+template <typename T, bool kDup, int TILE, int NW, int NS, int D>
+static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
+                              const KParams& kp, cudaStream_t stream, int dev) {
+  if (pl.ns != 0) return launch_kernel<T, kDup, TILE, NW, NS, D, true>(pl, mk, mv, kp, stream, dev);
+  return launch_kernel<T, kDup, TILE, NW, NS, D, false>(pl, mk, mv, kp, stream, dev);
 }
 
 template <typename T, bool kDup>

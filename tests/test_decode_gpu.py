@@ -166,6 +166,24 @@ def test_sweep_block_size_group(pa, oracle, dtype, bs, group):
     _check_workload(pa, oracle, w, num_splits=3)
 
 
+@pytest.mark.parametrize("group,bs,dtype", [(1, 16, torch.float16), (4, 16, torch.bfloat16),
+                                            (8, 32, torch.bfloat16), (2, 128, torch.float16)])
+def test_ragged_mixed_long_and_short_rows(pa, oracle, group, bs, dtype):
+    """Per-row lengths mixing rows that span several CTAs (cross-CTA merges)
+    with short rows (CTA boundaries moved to segment edges), every row checked."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(group * 1000 + bs)
+    b, hkv = 48, 2
+    lens = torch.randint(1, 120, (b,), generator=g, dtype=torch.int32)
+    long_rows = torch.randperm(b, generator=g)[:6]
+    lens[long_rows] = torch.randint(3000, 6000, (6,), generator=g, dtype=torch.int32)
+    lens[5] = 0
+    max_blocks = (6000 + bs - 1) // bs
+    w = workloads.build("ragged_mixed", b, hkv * group, hkv, bs, dtype, lens.cuda(), max_blocks,
+                        int(((lens + bs - 1) // bs).sum()) + 8, seed=group + bs, device="cuda")
+    _check_workload(pa, oracle, w)
+
+
 @pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
 @pytest.mark.parametrize("group,bs,dtype", [(1, 16, torch.float16), (4, 24, torch.bfloat16),
                                             (8, 128, torch.bfloat16), (3, 8, torch.float16)])
