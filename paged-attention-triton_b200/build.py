@@ -14,6 +14,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
@@ -23,14 +24,19 @@ HEADERS = [os.path.join(INCLUDE, "pa_decode.h"), os.path.join(HERE, "csrc", "fas
 OUTPUT = os.path.join(HERE, "paged_attention", "libpa_decode.so")
 EXT_SOURCE = os.path.join(HERE, "csrc", "torch_ext.cpp")
 EXT_OUTPUT = os.path.join(HERE, "paged_attention", "_pa_ext.so")
+BUILD_DIR = os.path.join(HERE, "_build")
+# pa_decode.cu compiles as parts in parallel: 0 = host API and small kernels,
+# 1-4 = decode-kernel instantiations (see the PA_PART blocks in the source).
+PARTS = (0, 1, 2, 3, 4)
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMPILE_FLAGS = ARCH_FLAGS + [
     "-lineinfo", "-O3", "-std=c++17",
-    "-shared", "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fPIC",
     "-Xcompiler", "-fvisibility=hidden",
-    "-cudart", "static",
+    "-diag-suppress", "177",          # constants unused by the host-only part
 ]
+LINK_FLAGS = ARCH_FLAGS + ["-shared", "-cudart", "static"]
 
 
 def _nvcc() -> str:
@@ -93,18 +99,31 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return OUTPUT
 
 
-def _build_library(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
-        return OUTPUT
-    cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", "-o", OUTPUT + ".tmp", *SOURCES]
+def _run(cmd, verbose):
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose and res.stderr:
         print(res.stderr, flush=True)
+
+
+def _build_library(force: bool = False, verbose: bool = False) -> str:
+    if not force and not _stale():
+        return OUTPUT
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    src = SOURCES[0]
+    objs = [os.path.join(BUILD_DIR, f"pa_decode_part{k}.o") for k in PARTS]
+    cmds = []
+    for k, obj in zip(PARTS, objs):
+        cmd = [_nvcc(), *COMPILE_FLAGS, f"-DPA_PART={k}", f"-I{INCLUDE}", "-c", "-o", obj, src]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+        cmds.append(cmd)
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as pool:
+        list(pool.map(lambda c: _run(c, verbose), cmds))
+    _run([_nvcc(), *LINK_FLAGS, "-o", OUTPUT + ".tmp", *objs], verbose)
     os.replace(OUTPUT + ".tmp", OUTPUT)
     return OUTPUT
 

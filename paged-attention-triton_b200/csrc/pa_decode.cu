@@ -34,6 +34,15 @@
 #include "pa_decode.h"
 #include "fastdiv.h"
 
+// The library can be compiled as one translation unit, or as parts in
+// parallel (build.py): part 0 holds the host API and the small kernels, parts
+// 1-4 instantiate the decode kernels (explicit instantiations at the end).
+#if !defined(PA_PART) || PA_PART == 0
+#define PA_HOST_PART 1
+#else
+#define PA_HOST_PART 0
+#endif
+
 namespace pa {
 
 constexpr int kCumMax = 1024;       // rows whose tile prefix sum fits in shared memory
@@ -1254,6 +1263,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
 }
 
+#if PA_HOST_PART
 // ----------------------------------------------------------------------------
 // ----------------------------------------------------------------------------
 // KV-cache append: one thread per 16-byte chunk of a K or V row
@@ -1392,6 +1402,8 @@ static int gcd_int(int a, int b) {
   return a;
 }
 
+#endif  // PA_HOST_PART
+
 // Kernel variants: tile tokens, worker warps per CTA, ring depth per warp.
 struct Variant {
   int tile, nw, ns;
@@ -1426,6 +1438,7 @@ struct Plan {
   size_t counters = 0;
 };
 
+#if PA_HOST_PART
 // Shared memory a variant needs before the group merge area.
 template <bool kDup, int TILE, int NW, int NS, int D>
 static int smem_base() {
@@ -1655,15 +1668,17 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+#endif  // PA_HOST_PART
 
 template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit>
-static cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
-                                 const KParams& kp, cudaStream_t stream, int dev) {
+cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
+                          const KParams& kp, cudaStream_t stream, int dev) {
   using C = Cfg<kDup, TILE, NW, NS, D>;
   static_assert(C::kSmemBase <= kMaxSmem, "shared memory plan exceeds 227 KB");
+  static std::mutex mu;
   static bool attr_set[64] = {false};
   {
-    std::lock_guard<std::mutex> lk(g_mu);
+    std::lock_guard<std::mutex> lk(mu);
     if (!attr_set[dev]) {
       const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1687,6 +1702,38 @@ static cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CU
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>, mk, mv, kp);
 }
+
+// Every decode kernel the dispatch below can launch, as (variant, layout) per
+// head_dim and dtype; PFX is `extern` for declarations, empty for definitions.
+#define PA_LK(T, DUP, TILE, NW, NS, D, SPLIT)                                               \
+  cudaError_t launch_kernel<T, DUP, TILE, NW, NS, D, SPLIT>(                                \
+      const Plan&, const CUtensorMap&, const CUtensorMap&, const KParams&, cudaStream_t, int)
+#define PA_BOTH(PFX, T, DUP, TILE, NW, NS, D)                 \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false);         \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, true);
+#define PA_D128(PFX, T)                                                              \
+  PA_BOTH(PFX, T, true, 32, 4, 3, 128) PA_BOTH(PFX, T, false, 32, 4, 3, 128)         \
+  PA_BOTH(PFX, T, true, 16, 8, 3, 128)                                               \
+  PA_BOTH(PFX, T, true, 32, 6, 2, 128) PA_BOTH(PFX, T, false, 32, 6, 2, 128)         \
+  PA_BOTH(PFX, T, true, 16, 12, 2, 128)                                              \
+  PA_BOTH(PFX, T, true, 16, 8, 2, 128) PA_BOTH(PFX, T, false, 16, 8, 2, 128)
+#define PA_D64(PFX, T)                                                               \
+  PA_BOTH(PFX, T, true, 32, 6, 2, 64) PA_BOTH(PFX, T, false, 32, 6, 2, 64)           \
+  PA_BOTH(PFX, T, true, 16, 8, 2, 64) PA_BOTH(PFX, T, false, 16, 8, 2, 64)
+#define PA_D256(PFX, T)                                                              \
+  PA_BOTH(PFX, T, true, 16, 4, 2, 256) PA_BOTH(PFX, T, false, 16, 4, 2, 256)         \
+  PA_BOTH(PFX, T, true, 16, 5, 2, 256) PA_BOTH(PFX, T, false, 16, 5, 2, 256)
+
+#if PA_HOST_PART
+#if defined(PA_PART)
+// Parts 1-4 hold the definitions.
+PA_D128(extern, __half)
+PA_D128(extern, __nv_bfloat16)
+PA_D64(extern, __half)
+PA_D64(extern, __nv_bfloat16)
+PA_D256(extern, __half)
+PA_D256(extern, __nv_bfloat16)
+#endif
 
 // The balanced and the split schedule are separate kernels: neither carries
 // the other's code (the kernels are bound by instruction fetch on short steps).
@@ -2012,3 +2059,18 @@ pa_status_t pa_stream_read(const void* src, size_t bytes, uint32_t* sink, cudaSt
 }
 
 }  // extern "C"
+
+#else  // decode-kernel parts (still inside namespace pa)
+#if PA_PART == 1
+PA_D128(, __half)
+#elif PA_PART == 2
+PA_D128(, __nv_bfloat16)
+#elif PA_PART == 3
+PA_D64(, __half)
+PA_D64(, __nv_bfloat16)
+#elif PA_PART == 4
+PA_D256(, __half)
+PA_D256(, __nv_bfloat16)
+#endif
+}  // namespace pa
+#endif  // PA_HOST_PART
