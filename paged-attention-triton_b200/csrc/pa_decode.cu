@@ -107,9 +107,7 @@ struct KParams {
   int R;                    // rows per TMA box (gcd(bs, TILE))
   int lspt;                 // log2(TILE / R): boxes per tile
   int lR;                   // log2(R)
-  int map5d;                // 1: one 5-D copy per box covers both 64-dim halves
   int W;                    // workers
-  int use_cum;              // balanced + seq_lens: prefix sums in shared memory
   int slot_cols;            // partial slot width: min(G, 8) query heads
   int gsz;                  // warps per merge group (NW, or 1 when the slots do not fit)
   int zero_rows;            // 1: some row may have length 0 (the output pre-pass runs)
@@ -168,15 +166,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
       if (mbar_try_wait(bar, parity)) return true;
     if (global_ns() - t0 > kWaitLimitNs) return false;
   }
-}
-
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            int c2, int c3, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
-      : "memory");
 }
 
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
@@ -308,8 +297,10 @@ __device__ __forceinline__ int clamp_len(const KParams& p, int s, bool& bad) {
   return s;
 }
 
+// Length of row b: the uniform length, or (kCum: per-row lengths) seq_lens[b].
+template <bool kCum>
 __device__ __forceinline__ int row_len(const KParams& p, int b) {
-  if (p.seq_lens == nullptr) return p.seq_len;
+  if constexpr (!kCum) return p.seq_len;
   bool bad = false;
   return clamp_len(p, __ldg(p.seq_lens + b), bad);
 }
@@ -343,13 +334,13 @@ struct Cursor {
   int seg_lo;         // unit index of the segment's tile 0 (balanced)
 };
 
-template <int TILE>
+template <int TILE, bool kCum>
 __device__ __forceinline__ void decode_unit(Cursor& c, const KParams& p, const int* cum, int u) {
   int row_base;
-  if (p.use_cum) {
+  if constexpr (kCum) {
     c.b = find_row(cum, p.B, u);
     row_base = cum[c.b];
-    c.S = row_len(p, c.b);
+    c.S = row_len<true>(p, c.b);
     c.nt = (c.S + TILE - 1) / TILE;
   } else {
     c.S = p.seq_len;
@@ -358,7 +349,7 @@ __device__ __forceinline__ void decode_unit(Cursor& c, const KParams& p, const i
     row_base = c.b * p.per_row;
   }
   const int r = u - row_base;
-  const int seg = p.use_cum ? r / c.nt : static_cast<int>(fast_div(static_cast<uint32_t>(r), p.div_nt));
+  const int seg = kCum ? r / c.nt : static_cast<int>(fast_div(static_cast<uint32_t>(r), p.div_nt));
   c.tile = r - seg * c.nt;
   c.kvh = p.QC == 1 ? seg : static_cast<int>(fast_div(static_cast<uint32_t>(seg), p.div_qc));
   c.qc = seg - c.kvh * p.QC;
@@ -366,7 +357,7 @@ __device__ __forceinline__ void decode_unit(Cursor& c, const KParams& p, const i
 }
 
 // Next unit in flattened order (balanced).
-template <int TILE>
+template <int TILE, bool kCum>
 __device__ __forceinline__ void cursor_next(Cursor& c, const KParams& p) {
   if (++c.tile < c.nt) return;
   c.tile = 0;
@@ -378,7 +369,7 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const KParams& p) {
   do {   // next row that owns tiles (rows of length 0 own none)
     if (c.b + 1 >= p.B) { c.nt = 1; return; }   // past the end: never used
     ++c.b;
-    c.S = row_len(p, c.b);
+    c.S = row_len<kCum>(p, c.b);
     c.nt = (c.S + TILE - 1) / TILE;
   } while (c.nt == 0);
 }
@@ -413,7 +404,7 @@ __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
 // serves box (L & (spt-1)) of tile (L >> lspt) of the batch [u0, u1) (units of
 // the warp range, or tile ordinals of a split). INT_MIN: the box holds no token
 // of its piece (not loaded; the consumer masks it). One load per lane.
-template <int TILE, bool kSplit>
+template <int TILE, bool kSplit, bool kCum>
 __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, const Ranges& rg,
                                             const Work& w, int u0, int u1, int lane, int& phys,
                                             int& slot) {
@@ -425,7 +416,7 @@ __device__ __forceinline__ void batch_pages(const KParams& p, const int* cum, co
     int tile, b, t0, t1;
     if constexpr (!kSplit) {
       Cursor c;
-      decode_unit<TILE>(c, p, cum, u0 + ord);
+      decode_unit<TILE, kCum>(c, p, cum, u0 + ord);
       int fl;
       piece_of<TILE>(c, rg, t0, t1, fl);
       tile = c.tile;
@@ -675,7 +666,7 @@ __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
-template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum>
 __global__ void __launch_bounds__(NW * 32, 1)
     pa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const KParams p) {
@@ -726,7 +717,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
   };
   // Same-length rows: the ranges need no memory, so they are set before the wait.
-  if (!kSplit && !p.use_cum) set_ranges(p.U, p.P, p.Pw);
+  if (!kSplit && !kCum) set_ranges(p.U, p.P, p.Pw);
 
   // Programmatic dependent launch: everything above touches no global memory;
   // from here on the kernel reads inputs (and writes outputs, partials and
@@ -734,7 +725,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // Balanced schedule with per-row lengths: per-row tile prefix sums.
-  if (!kSplit && p.use_cum) {
+  if (!kSplit && kCum) {
     const int B = p.B;
     const int nseg = p.Hkv * p.QC;
     const int chunk = (B + blockDim.x - 1) / blockDim.x;
@@ -770,7 +761,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
   if (!kSplit && p.zero_rows) {
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-      if (row_len(p, b) != 0) continue;
+      if (row_len<kCum>(p, b) != 0) continue;
       for (int idx = threadIdx.x; idx < p.Hq * (D / 8); idx += blockDim.x) {
         const int h = idx / (D / 8), c = idx % (D / 8);
         *reinterpret_cast<uint4*>(p.out + b * p.o_sb + h * p.o_sh + c * 16) =
@@ -788,7 +779,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   w.b = w.kvh = w.qc = w.s = w.t0 = w.t1 = w.tl0 = w.n = 0;
   int n_tiles = 0;
   if (!kSplit) {
-    if (p.use_cum) {
+    if (kCum) {
       const int U = cum[p.B];
       const int P = max(static_cast<int>(fast_div(static_cast<uint32_t>(U) + p.div_ng.d - 1,
                                                   p.div_ng)),
@@ -850,14 +841,14 @@ __global__ void __launch_bounds__(NW * 32, 1)
   int u0c = range0, u1c = min(range1, range0 + bt_tiles);
   int u0n = u1c, u1n = min(range1, u1c + bt_tiles);
   int pg_c = INT_MIN, sl_c = 0, pg_n = INT_MIN, sl_n = 0;
-  if (u0c < u1c) batch_pages<TILE, kSplit>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
+  if (u0c < u1c) batch_pages<TILE, kSplit, kCum>(p, cum, rg, w, u0c, u1c, lane, pg_c, sl_c);
   Cursor ic;
   ic.b = w.b;
   ic.kvh = w.kvh;
   ic.qc = w.qc;
   ic.tile = w.tl0;
   ic.nt = ic.S = ic.seg_lo = 0;
-  if (!kSplit && n_tiles > 0) decode_unit<TILE>(ic, p, cum, range0);
+  if (!kSplit && n_tiles > 0) decode_unit<TILE, kCum>(ic, p, cum, range0);
   int ord = 0;          // tile ordinal within the current batch
   int issued = 0;
 
@@ -896,16 +887,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     if (valid) {
       const uint32_t hs = p.R * 128;                     // one chunk of one box
       const uint32_t dk = sk + lane * H::kChunks * hs;   // this lane's box
-      if (p.map5d) {
-        tma_load_5d(dk, &tmK, 0, pslot, 0, ic.kvh, phys, bar);
-        tma_load_5d(dk + C::kKV, &tmV, 0, pslot, 0, ic.kvh, phys, bar);
-      } else {
-#pragma unroll
-        for (int c = 0; c < H::kChunks; ++c) {
-          tma_load_4d(dk + c * hs, &tmK, 64 * c, ic.kvh, pslot, phys, bar);
-          tma_load_4d(dk + C::kKV + c * hs, &tmV, 64 * c, ic.kvh, pslot, phys, bar);
-        }
-      }
+      tma_load_5d(dk, &tmK, 0, pslot, 0, ic.kvh, phys, bar);
+      tma_load_5d(dk + C::kKV, &tmV, 0, pslot, 0, ic.kvh, phys, bar);
     }
     if (first && lane < gc) {
       const int hq = ic.kvh * G + ic.qc * 8 + lane;
@@ -913,7 +896,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     ++issued;
     // advance to the next tile
-    if (!kSplit) cursor_next<TILE>(ic, p); else ++ic.tile;
+    if (!kSplit) cursor_next<TILE, kCum>(ic, p); else ++ic.tile;
     if (u0c + ++ord < u1c) return;
     u0c = u0n;
     u1c = u1n;
@@ -922,7 +905,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     ord = 0;
     u0n = u1c;
     u1n = min(range1, u1c + bt_tiles);
-    if (u0n < u1n) batch_pages<TILE, kSplit>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
+    if (u0n < u1n) batch_pages<TILE, kSplit, kCum>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   };
 
   for (int s = 0; s < NS && issued < n_tiles; ++s) issue(s);
@@ -930,7 +913,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // batch holds at least 8 tiles (32 boxes of >= 8 rows), more than the NS
   // issued above, so those never reached it (a range that ended inside the
   // first batch has no second one).
-  if (u0n < u1n) batch_pages<TILE, kSplit>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
+  if (u0n < u1n) batch_pages<TILE, kSplit, kCum>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   if (!kSplit) __syncthreads();   // gcnt is zero for every warp's merges
   // The next kernel in the stream may start its own prologue on SMs this grid
   // leaves; it waits for this grid's completion before touching memory.
@@ -1567,47 +1550,29 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
   return PA_OK;
 }
 
-// Tensor map of one paged cache [num_blocks, block_size, Hkv, D]. The 5-D form
-// orders the dimensions (64 dims, slot, 64-dim chunk, head, block) so that one
+// Tensor map of one paged cache [num_blocks, block_size, Hkv, D], with the
+// dimensions ordered (64 dims, slot, 64-dim chunk, head, block) so that one
 // box of {64, R, D/64, 1, 1} lands as [chunk][R rows][128 B]: all chunks of R
-// token rows in one copy. The 4-D form {D dims, head, slot, block} with box
-// {64, 1, R, 1} needs one copy per chunk.
+// token rows in one copy. The strides are the caller's (multiples of 16 bytes).
 static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const void* base,
-                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows,
-                             bool five_d) {
+                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   const CUtensorMapDataType dt =
       p->dtype == PA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r;
-  if (five_d) {
-    cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(p->block_size),
-                          static_cast<cuuint64_t>(p->head_dim / 64),
-                          static_cast<cuuint64_t>(p->num_kv_heads),
-                          static_cast<cuuint64_t>(p->num_blocks)};
-    cuuint64_t strides[4] = {static_cast<cuuint64_t>(s_slot) * 2, 128,
-                             static_cast<cuuint64_t>(s_head) * 2,
-                             static_cast<cuuint64_t>(s_block) * 2};
-    cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows),
-                         static_cast<cuuint32_t>(p->head_dim / 64), 1, 1};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    r = fn(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  } else {
-    cuuint64_t dims[4] = {static_cast<cuuint64_t>(p->head_dim),
-                          static_cast<cuuint64_t>(p->num_kv_heads),
-                          static_cast<cuuint64_t>(p->block_size),
-                          static_cast<cuuint64_t>(p->num_blocks)};
-    cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2,
-                             static_cast<cuuint64_t>(s_slot) * 2,
-                             static_cast<cuuint64_t>(s_block) * 2};
-    cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  }
+  cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(p->block_size),
+                        static_cast<cuuint64_t>(p->head_dim / 64),
+                        static_cast<cuuint64_t>(p->num_kv_heads),
+                        static_cast<cuuint64_t>(p->num_blocks)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(s_slot) * 2, 128,
+                           static_cast<cuuint64_t>(s_head) * 2,
+                           static_cast<cuuint64_t>(s_block) * 2};
+  cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows),
+                       static_cast<cuuint32_t>(p->head_dim / 64), 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = fn(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1615,13 +1580,12 @@ static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const 
 // K/V cache pointers every step. Small round-robin cache, keyed by everything
 // the encoding depends on.
 struct MapKey {
-  int dev, dtype, rows, five_d, head_dim;
+  int dev, dtype, rows, head_dim;
   const void* base;
   int64_t dims[3];      // block_size, num_kv_heads, num_blocks
   int64_t strides[3];   // block, slot, head (elements)
   bool operator==(const MapKey& o) const {
-    return dev == o.dev && dtype == o.dtype && rows == o.rows && five_d == o.five_d &&
-           head_dim == o.head_dim &&
+    return dev == o.dev && dtype == o.dtype && rows == o.rows && head_dim == o.head_dim &&
            base == o.base && memcmp(dims, o.dims, sizeof(dims)) == 0 &&
            memcmp(strides, o.strides, sizeof(strides)) == 0;
   }
@@ -1633,14 +1597,12 @@ static bool g_map_valid[kMapCache];
 static int g_map_next = 0;
 
 static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int dev, const void* base,
-                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows,
-                             bool five_d) {
+                             int64_t s_block, int64_t s_slot, int64_t s_head, int rows) {
   MapKey key;
   memset(&key, 0, sizeof(key));
   key.dev = dev;
   key.dtype = p->dtype;
   key.rows = rows;
-  key.five_d = five_d ? 1 : 0;
   key.head_dim = p->head_dim;
   key.base = base;
   key.dims[0] = p->block_size;
@@ -1657,7 +1619,7 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
         return true;
       }
   }
-  if (!encode_cache_map(map, p, base, s_block, s_slot, s_head, rows, five_d)) return false;
+  if (!encode_cache_map(map, p, base, s_block, s_slot, s_head, rows)) return false;
   std::lock_guard<std::mutex> lk(g_mu);
   const int i = g_map_next;
   g_map_next = (g_map_next + 1) % kMapCache;
@@ -1670,7 +1632,7 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 #endif  // PA_HOST_PART
 
-template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum>
 cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                           const KParams& kp, cudaStream_t stream, int dev) {
   using C = Cfg<kDup, TILE, NW, NS, D>;
@@ -1680,7 +1642,7 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>,
+      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kMaxSmem);
       if (e != cudaSuccess) return e;
@@ -1700,17 +1662,18 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit>, mk, mv, kp);
+  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>, mk, mv, kp);
 }
 
 // Every decode kernel the dispatch below can launch, as (variant, layout) per
 // head_dim and dtype; PFX is `extern` for declarations, empty for definitions.
-#define PA_LK(T, DUP, TILE, NW, NS, D, SPLIT)                                               \
-  cudaError_t launch_kernel<T, DUP, TILE, NW, NS, D, SPLIT>(                                \
+#define PA_LK(T, DUP, TILE, NW, NS, D, SPLIT, CUM)                                          \
+  cudaError_t launch_kernel<T, DUP, TILE, NW, NS, D, SPLIT, CUM>(                           \
       const Plan&, const CUtensorMap&, const CUtensorMap&, const KParams&, cudaStream_t, int)
 #define PA_BOTH(PFX, T, DUP, TILE, NW, NS, D)                 \
-  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false);         \
-  PFX template PA_LK(T, DUP, TILE, NW, NS, D, true);
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, false);  \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, true);   \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, true, false);
 #define PA_D128(PFX, T)                                                              \
   PA_BOTH(PFX, T, true, 32, 4, 3, 128) PA_BOTH(PFX, T, false, 32, 4, 3, 128)         \
   PA_BOTH(PFX, T, true, 16, 8, 3, 128)                                               \
@@ -1735,13 +1698,17 @@ PA_D256(extern, __half)
 PA_D256(extern, __nv_bfloat16)
 #endif
 
-// The balanced and the split schedule are separate kernels: neither carries
-// the other's code (the kernels are bound by instruction fetch on short steps).
+// The split schedule, the balanced schedule over same-length rows and the
+// balanced schedule over per-row lengths are separate kernels: none carries
+// another's code (short steps are bound by instruction fetch).
 template <typename T, bool kDup, int TILE, int NW, int NS, int D>
 static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                               const KParams& kp, cudaStream_t stream, int dev) {
-  if (pl.ns != 0) return launch_kernel<T, kDup, TILE, NW, NS, D, true>(pl, mk, mv, kp, stream, dev);
-  return launch_kernel<T, kDup, TILE, NW, NS, D, false>(pl, mk, mv, kp, stream, dev);
+  if (pl.ns != 0)
+    return launch_kernel<T, kDup, TILE, NW, NS, D, true, false>(pl, mk, mv, kp, stream, dev);
+  if (pl.use_cum)
+    return launch_kernel<T, kDup, TILE, NW, NS, D, false, true>(pl, mk, mv, kp, stream, dev);
+  return launch_kernel<T, kDup, TILE, NW, NS, D, false, false>(pl, mk, mv, kp, stream, dev);
 }
 
 template <typename T, bool kDup>
@@ -1887,7 +1854,6 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   for (int k = 0; k < 31; ++k)
     if ((1 << k) == p->block_size) kp.bs_log2 = k;
   kp.W = pl.W;
-  kp.use_cum = pl.use_cum ? 1 : 0;
   kp.slot_cols = pl.slot_cols;
   kp.gsz = pl.gsz;
   kp.zero_rows = (p->seq_lens != nullptr || p->seq_len == 0) ? 1 : 0;
@@ -1916,18 +1882,11 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
 
   CUtensorMap mk, mv;
-  kp.map5d = 1;
   if (!cached_cache_map(&mk, p, dev, p->k_cache, p->k_stride_block, p->k_stride_slot,
-                        p->k_stride_head, kp.R, true) ||
+                        p->k_stride_head, kp.R) ||
       !cached_cache_map(&mv, p, dev, p->v_cache, p->v_stride_block, p->v_stride_slot,
-                        p->v_stride_head, kp.R, true)) {
-    kp.map5d = 0;
-    if (!cached_cache_map(&mk, p, dev, p->k_cache, p->k_stride_block, p->k_stride_slot,
-                          p->k_stride_head, kp.R, false) ||
-        !cached_cache_map(&mv, p, dev, p->v_cache, p->v_stride_block, p->v_stride_slot,
-                          p->v_stride_head, kp.R, false))
-      return PA_ERR_ARG;
-  }
+                        p->v_stride_head, kp.R))
+    return PA_ERR_ARG;
 
   cudaError_t e;
   if (p->dtype == PA_F16)
