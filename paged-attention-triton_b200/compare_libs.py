@@ -1,6 +1,11 @@
 """Same-GPU comparison with library paged-attention decode kernels.
 
     python compare_libs.py [--configs c1,c2,c3,c4,c5] [--iters 50]
+    python compare_libs.py --head-dims 64,256 [--iters 50]
+
+``--head-dims`` runs C2-sized MHA steps (B=32, S=1024, block 16, fp16, 537 MB
+of K/V) at other head dimensions instead of the five configurations (query
+heads chosen so the bytes match: 64 heads at D=64, 16 at D=256).
 
 For each benchmark shape it times this operator, vLLM's
 ``paged_attention_v1`` / ``paged_attention_v2`` (the kernels the reference's
@@ -120,7 +125,7 @@ def _flashinfer_runner(w, lens_list, scale):
     wrapper = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, "NHD",
                                                             use_tensor_cores=w.num_heads != w.num_kv_heads)
     wrapper.plan(torch.tensor(indptr, dtype=torch.int32, device="cuda"), indices.cuda(),
-                 last.cuda(), w.num_heads, w.num_kv_heads, 128, bs, q_data_type=q.dtype,
+                 last.cuda(), w.num_heads, w.num_kv_heads, q.shape[-1], bs, q_data_type=q.dtype,
                  kv_data_type=k.dtype, sm_scale=scale)
 
     def run():
@@ -132,14 +137,24 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5")
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--head-dims", default="", help="e.g. 64,256: C2-sized MHA at these D")
     a = ap.parse_args()
     flush = _Flush()
-    for name in a.configs.split(","):
-        w = workloads.CONFIGS[name]("cuda")
+    if a.head_dims:
+        heads = {64: 64, 128: 32, 256: 16}
+        builders = [(f"c2size_d{d}", (lambda d=d: workloads.build(
+            f"c2size_mha_d{d}_h{heads[d]}_s1024_bs16_f16", 32, heads[d], heads[d], 16,
+            torch.float16, 1024, 64, 2048, 2, "cuda", head_dim=d)))
+            for d in (int(x) for x in a.head_dims.split(","))]
+    else:
+        builders = [(name, (lambda name=name: workloads.CONFIGS[name]("cuda")))
+                    for name in a.configs.split(",")]
+    for name, make in builders:
+        w = make()
         lens_list = w.seq_list()
         lens = torch.tensor(lens_list, dtype=torch.int32, device="cuda")
         max_s = max(lens_list)
-        scale = 1.0 / math.sqrt(128)
+        scale = 1.0 / math.sqrt(w.q.shape[-1])
         ws = pa.DecodeWorkspace("cuda")
         mine_out = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
                                       w.block_size, workspace=ws)
