@@ -96,9 +96,9 @@ typedef struct pa_decode_params {
   int32_t* counters;           /* zero-filled once by the caller; the kernel leaves it zeroed */
   size_t counter_count;
   uint32_t* status;            /* optional device word, PA_STATUS_* bits OR-ed in */
-  /* 0: automatic. 1..7: a fixed kernel variant (tile tokens x warps x ring
+  /* 0: automatic. 1..9: a fixed kernel variant (tile tokens x warps x ring
    * depth), for tuning; see the variant table in csrc/pa_decode.cu (1-5 for
-   * head_dim 128, 3 and 5 for 64, 6 and 7 for 256; others return
+   * head_dim 128; 3, 5 and 8 for 64; 6, 7 and 9 for 256; others return
    * PA_ERR_UNSUPPORTED). */
   int32_t kernel_variant;
 } pa_decode_params;

@@ -1399,6 +1399,8 @@ static const Variant kVariants[] = {
     {16, 8, 2},   // 5 (head_dim 64 or 128)
     {16, 4, 2},   // 6 (head_dim 256: 16 KB K+V tiles)
     {16, 5, 2},   // 7 (head_dim 256)
+    {64, 6, 2},   // 8 (head_dim 64: 16 KB K+V tiles)
+    {32, 3, 2},   // 9 (head_dim 256: 32 KB K+V tiles)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // Opt-in shared memory per CTA is 227 KB (232448 B), static plus dynamic; the
@@ -1431,9 +1433,9 @@ static int smem_base() {
 // Whether (head_dim, variant, layout) is instantiated.
 static bool variant_built(int D, int variant, bool dup) {
   switch (D) {
-    case 64: return variant == 3 || variant == 5;
+    case 64: return variant == 3 || variant == 5 || variant == 8;
     case 128: return variant >= 1 && variant <= 5 && (dup || (variant != 2 && variant != 4));
-    case 256: return variant == 6 || variant == 7;
+    case 256: return variant == 6 || variant == 7 || variant == 9;
     default: return false;
   }
 }
@@ -1441,10 +1443,12 @@ static bool variant_built(int D, int variant, bool dup) {
 static int variant_smem_base(int variant, bool dup, int D) {
   if (D == 64) {
     if (variant == 3) return dup ? smem_base<true, 32, 6, 2, 64>() : smem_base<false, 32, 6, 2, 64>();
+    if (variant == 8) return dup ? smem_base<true, 64, 6, 2, 64>() : smem_base<false, 64, 6, 2, 64>();
     return dup ? smem_base<true, 16, 8, 2, 64>() : smem_base<false, 16, 8, 2, 64>();
   }
   if (D == 256) {
     if (variant == 7) return dup ? smem_base<true, 16, 5, 2, 256>() : smem_base<false, 16, 5, 2, 256>();
+    if (variant == 9) return dup ? smem_base<true, 32, 3, 2, 256>() : smem_base<false, 32, 3, 2, 256>();
     return dup ? smem_base<true, 16, 4, 2, 256>() : smem_base<false, 16, 4, 2, 256>();
   }
   switch (variant) {
@@ -1485,18 +1489,18 @@ static pa_status_t validate(const pa_decode_params* p) {
 // Automatic choice, from B200 sweeps. head_dim 128 (the five benchmark
 // shapes): MHA with pages shorter than 32 tokens, and groups larger than 4
 // query heads, stream best as 16-token tiles on 8 warps; longer pages and 2- or
-// 4-head groups as 32-token tiles on 6 warps. head_dim 64: 32-token tiles on 6
-// warps throughout. head_dim 256: 16-token tiles on 5 warps, or 4 warps when
-// the query columns cannot be duplicated (the merge area of 5 warps x 8
-// columns does not fit).
+// 4-head groups as 32-token tiles on 6 warps. head_dim 64 (128-byte rows):
+// MHA as 32-token tiles on 6 warps, query-head groups as 64-token tiles on 6
+// warps. head_dim 256: MHA as 16-token tiles on 5 warps, groups as 32-token
+// tiles on 3 warps.
 static int pick_variant(const pa_decode_params* p, bool dup) {
   int v = p->kernel_variant;
   if (v == 0) {
     const int g = p->num_heads / p->num_kv_heads;
     if (p->head_dim == 256)
-      v = dup ? 7 : 6;      // 5 warps where their merge area fits (up to 4 query columns)
+      v = g == 1 ? 7 : 9;   // MHA: 16-token tiles on 5 warps; groups: 32-token tiles on 3
     else if (p->head_dim == 64)
-      v = 3;                // 32-token tiles of 128-byte rows
+      v = g == 1 ? 3 : 8;   // MHA: 32-token tiles on 6 warps; groups: 64-token tiles
     else
       v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
   }
@@ -1570,9 +1574,13 @@ static bool encode_cache_map(CUtensorMap* map, const pa_decode_params* p, const 
   cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows),
                        static_cast<cuuint32_t>(p->head_dim / 64), 1, 1};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  // L2 fills widened to 256 B suit rows of >= 256 B; a 128-byte row (D = 64)
+  // would drag its neighbouring head's row along.
+  const CUtensorMapL2promotion promo = p->head_dim == 64 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                                                         : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
   const CUresult r = fn(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1682,10 +1690,12 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   PA_BOTH(PFX, T, true, 16, 8, 2, 128) PA_BOTH(PFX, T, false, 16, 8, 2, 128)
 #define PA_D64(PFX, T)                                                               \
   PA_BOTH(PFX, T, true, 32, 6, 2, 64) PA_BOTH(PFX, T, false, 32, 6, 2, 64)           \
-  PA_BOTH(PFX, T, true, 16, 8, 2, 64) PA_BOTH(PFX, T, false, 16, 8, 2, 64)
+  PA_BOTH(PFX, T, true, 16, 8, 2, 64) PA_BOTH(PFX, T, false, 16, 8, 2, 64)           \
+  PA_BOTH(PFX, T, true, 64, 6, 2, 64) PA_BOTH(PFX, T, false, 64, 6, 2, 64)
 #define PA_D256(PFX, T)                                                              \
   PA_BOTH(PFX, T, true, 16, 4, 2, 256) PA_BOTH(PFX, T, false, 16, 4, 2, 256)         \
-  PA_BOTH(PFX, T, true, 16, 5, 2, 256) PA_BOTH(PFX, T, false, 16, 5, 2, 256)
+  PA_BOTH(PFX, T, true, 16, 5, 2, 256) PA_BOTH(PFX, T, false, 16, 5, 2, 256)         \
+  PA_BOTH(PFX, T, true, 32, 3, 2, 256) PA_BOTH(PFX, T, false, 32, 3, 2, 256)
 
 #if PA_HOST_PART
 #if defined(PA_PART)
@@ -1716,10 +1726,12 @@ static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorM
                           const KParams& kp, cudaStream_t stream, int dev) {
   if (pl.D == 64) {
     if (pl.variant == 3) return launch_one<T, kDup, 32, 6, 2, 64>(pl, mk, mv, kp, stream, dev);
+    if (pl.variant == 8) return launch_one<T, kDup, 64, 6, 2, 64>(pl, mk, mv, kp, stream, dev);
     return launch_one<T, kDup, 16, 8, 2, 64>(pl, mk, mv, kp, stream, dev);
   }
   if (pl.D == 256) {
     if (pl.variant == 7) return launch_one<T, kDup, 16, 5, 2, 256>(pl, mk, mv, kp, stream, dev);
+    if (pl.variant == 9) return launch_one<T, kDup, 32, 3, 2, 256>(pl, mk, mv, kp, stream, dev);
     return launch_one<T, kDup, 16, 4, 2, 256>(pl, mk, mv, kp, stream, dev);
   }
   switch (pl.variant) {

@@ -100,7 +100,7 @@ def test_zero_length_and_empty_split_head_dim(pa, head_dim):
     assert torch.equal(lse_p[1, :, 3].cpu(), SENTINEL.expand(8))
 
 
-@pytest.mark.parametrize("variant", [3, 5])
+@pytest.mark.parametrize("variant", [3, 5, 8])
 @pytest.mark.parametrize("group", [1, 4, 8])
 def test_head_dim_64_variants(pa, oracle, variant, group):
     from paged_attention import workloads
@@ -112,7 +112,7 @@ def test_head_dim_64_variants(pa, oracle, variant, group):
     _check(pa, oracle, w, num_splits=5, kernel_variant=variant)
 
 
-@pytest.mark.parametrize("variant", [6, 7])
+@pytest.mark.parametrize("variant", [6, 7, 9])
 @pytest.mark.parametrize("group", [1, 4, 8])
 def test_head_dim_256_variants(pa, oracle, variant, group):
     from paged_attention import workloads
