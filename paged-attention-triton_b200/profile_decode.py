@@ -29,8 +29,13 @@ def main():
     ap.add_argument("--num-splits", type=int, default=0)
     ap.add_argument("--flush", action="store_true")
     ap.add_argument("--variant", type=int, default=0, help="kernel variant (0 = automatic)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="c5 only: the first N of its 256 rows (a smaller shard for profiling)")
     a = ap.parse_args()
-    w = workloads.CONFIGS[a.config]("cuda")
+    if a.batch and a.config == "c5":
+        w = workloads.c5("cuda", batch=a.batch)
+    else:
+        w = workloads.CONFIGS[a.config]("cuda")
     ws = pa.DecodeWorkspace("cuda")
     wbuf = torch.empty(512 << 20, dtype=torch.uint8, device="cuda") if a.flush else None
     rbuf = torch.ones(128 << 20, dtype=torch.int32, device="cuda") if a.flush else None
