@@ -1,0 +1,108 @@
+"""GPU edge shapes: wide query-head groups, one very long sequence (a segment
+spread over many CTAs: the general cross-CTA merge), more ragged rows than the
+per-CTA prefix sum holds (the plan falls back to the split schedule), large
+pages, and caches with padded strides. Every case against the oracle.
+"""
+import pytest
+import torch
+
+from helpers import assert_lse_close, assert_o_close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def pa():
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+    import paged_attention
+    return paged_attention
+
+
+@pytest.fixture(scope="module")
+def oracle():
+    import oracle as o
+    return o
+
+
+def _run_and_check(pa, oracle, q, k, v, bt, lens, bs, rows=None, num_splits=None):
+    ws = pa.DecodeWorkspace(q.device)
+    o, lse = pa.paged_attention(q, k, v, bt, lens, bs, num_splits, return_lse=True, workspace=ws)
+    torch.cuda.synchronize()
+    assert ws.read_status() == 0
+    ro, rl = oracle.decode_reference(q, k, v, bt, lens, bs, batch_indices=rows)
+    if rows is not None:
+        idx = torch.tensor(rows)
+        o, lse, ro, rl = o.cpu()[idx], lse.cpu()[idx], ro[idx], rl[idx]
+    assert_o_close(o, ro, "O")
+    assert_lse_close(lse, rl, "LSE")
+
+
+@pytest.mark.parametrize("hq,hkv", [(64, 1), (32, 1), (24, 2)])
+def test_wide_query_groups(pa, oracle, hq, hkv):
+    """G = 64, 32, 12: several chunks of 8 query heads per KV head."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(hq)
+    lens = torch.randint(0, 700, (9,), generator=g, dtype=torch.int32)
+    w = workloads.build("wide_g", 9, hq, hkv, 16, torch.bfloat16, lens.cuda(), 44, 9 * 44,
+                        seed=hq, device="cuda")
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, lens.cuda(), 16)
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, 650, 16)
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, 650, 16, num_splits=4)
+
+
+@pytest.mark.parametrize("hq,hkv,dtype", [(8, 8, torch.float16), (32, 4, torch.bfloat16)])
+def test_one_long_sequence(pa, oracle, hq, hkv, dtype):
+    """B = 1, S = 131072: each KV head's segment spans many CTAs, so its pieces
+    merge through the general (more than 8 rows) cross-CTA path."""
+    from paged_attention import workloads
+    s, bs = 131072, 16
+    w = workloads.build("long_seq", 1, hq, hkv, bs, dtype, s, s // bs, s // bs, seed=hq,
+                        device="cuda")
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, s, bs)
+    lens = torch.tensor([s - 77], dtype=torch.int32, device="cuda")
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, lens, bs)
+
+
+def test_more_ragged_rows_than_prefix_sum(pa, oracle):
+    """1500 rows with per-row lengths (over the 1024-row prefix sum): the plan
+    runs the split schedule with the reference heuristic; sampled rows."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(3)
+    b = 1500
+    lens = torch.randint(0, 96, (b,), generator=g, dtype=torch.int32)
+    w = workloads.build("many_rows", b, 8, 2, 16, torch.float16, lens.cuda(), 6, b * 6,
+                        seed=3, device="cuda")
+    rows = [0, 1, 511, 1023, 1024, 1499]
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, lens.cuda(), 16,
+                   rows=rows)
+
+
+@pytest.mark.parametrize("bs", [256, 512])
+@pytest.mark.parametrize("group", [1, 8])
+def test_large_pages(pa, oracle, bs, group):
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(bs + group)
+    lens = torch.randint(1, 3 * bs, (5,), generator=g, dtype=torch.int32)
+    w = workloads.build("large_pages", 5, 2 * group, 2, bs, torch.bfloat16, lens.cuda(), 3, 20,
+                        seed=bs, device="cuda")
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, lens.cuda(), bs)
+    _run_and_check(pa, oracle, w.q, w.k_cache, w.v_cache, w.block_table, 2 * bs + 5, bs,
+                   num_splits=3)
+
+
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
+def test_padded_cache_strides(pa, oracle, head_dim):
+    """K/V views with padded head and slot strides (head dimension contiguous)."""
+    g = torch.Generator(device="cuda").manual_seed(head_dim)
+    nb, bs, hkv, hq, b, s = 32, 16, 2, 8, 3, 150
+    pad_d, pad_h = head_dim + 32, hkv + 1
+    kbuf = torch.randn(nb, bs, pad_h, pad_d, generator=g, device="cuda").to(torch.bfloat16)
+    vbuf = torch.randn(nb, bs, pad_h, pad_d, generator=g, device="cuda").to(torch.bfloat16)
+    k = kbuf[:, :, :hkv, :head_dim]
+    v = vbuf[:, :, :hkv, :head_dim]
+    assert k.stride(3) == 1 and not k.is_contiguous()
+    q = torch.randn(b, hq, head_dim, generator=g, device="cuda").to(torch.bfloat16)
+    bt = torch.randperm(nb, generator=g, device="cuda")[: b * 10].reshape(b, 10).int()
+    _run_and_check(pa, oracle, q, k, v, bt, s, bs)
+    _run_and_check(pa, oracle, q, k, v, bt, s, bs, num_splits=2)
