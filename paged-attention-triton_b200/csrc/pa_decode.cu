@@ -109,7 +109,8 @@ struct KParams {
   int lR;                   // log2(R)
   int W;                    // workers
   int slot_cols;            // partial slot width: min(G, 8) query heads
-  int gsz;                  // warps per merge group (NW, or 1 when the slots do not fit)
+  int gsz;                  // warps per merge group (NW, or 1 for short segments whose
+                            // merge rows do not fit in shared memory)
   int zero_rows;            // 1: some row may have length 0 (the output pre-pass runs)
   // Balanced schedule, computed on the host: the unit count and range sizes
   // (valid when every row has the same length), and the launch-invariant
@@ -121,6 +122,7 @@ struct KParams {
   FastDiv div_qc;           // by QC
   FastDiv div_bs;           // by bs (pages that are not a power of two)
   FastDiv div_ng;           // by the number of groups (P with per-row lengths)
+  float* wslots;            // warps' merge rows in global memory (null: shared memory)
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -680,7 +682,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
   int* descs = reinterpret_cast<int*>(smem + C::kDescOff);
   int* cum = reinterpret_cast<int*>(smem + C::kCumOff);
   int* gcnt = reinterpret_cast<int*>(smem + C::kGroupOff);         // [NW] arrival counters
-  float* gslots = reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
+  // The warps' merge rows ([NW][2][slot_cols][D + 4] floats per CTA): shared
+  // memory when they fit beside the stages, else this CTA's part of the
+  // workspace (same-CTA writers and reader, ordered by the CTA-scope fences).
+  float* gslots = p.wslots ? p.wslots + static_cast<size_t>(blockIdx.x) * NW * 2 * p.slot_cols *
+                                            H::kSlotStride
+                           : reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
   __shared__ int warp_tot[NW];
 
   const int warp = threadIdx.x >> 5;
@@ -1416,6 +1423,7 @@ struct Plan {
   bool dup = true;
   int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
+  bool wslot_global = false;   // balanced: warps' merge rows in the workspace
   int slot_cols = 1;
   int gsz = 1;             // balanced: warps per merge group
   int smem = 0;            // dynamic shared memory of the launch
@@ -1503,9 +1511,25 @@ static int pick_variant(const pa_decode_params* p, bool dup) {
       v = g == 1 ? 3 : 8;   // MHA: 32-token tiles on 6 warps; groups: 64-token tiles
     else
       v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
+    // 32x6x2 keeps its warps' merge rows in shared memory only up to 2 query
+    // columns; with more, and segments that can exceed 8 tiles, 16x8x2 (whose
+    // merge rows fit) wins over merging through the workspace.
+    if (v == 3 && p->head_dim == 128) {
+      const int cols = std::min(g, 8);
+      const bool fits = variant_smem_base(3, dup, 128) + 6 * 2 * (128 + 4) * 4 * cols <= kMaxSmem;
+      const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
+      if (!fits && (cap + 31) / 32 > 8) v = 5;
+    }
   }
   if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
   return variant_built(p->head_dim, v, dup) ? v : 0;   // 0: not built for this head_dim
+}
+
+// Bytes of the balanced schedule's group partials (rows, then LSEs), rounded
+// to 16 bytes so that what follows stays aligned.
+static size_t group_slot_bytes(const Plan& pl, size_t slots) {
+  const size_t b = slots * pl.slot_cols * (pl.D + 1) * sizeof(float);
+  return (b + 15) & ~size_t(15);
 }
 
 static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
@@ -1536,11 +1560,24 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     pl.use_cum = p->seq_lens != nullptr;
     // Merge pieces inside a CTA through shared memory when the warps' rows fit.
     const int base = variant_smem_base(pl.variant, pl.dup, pl.D);
+    // Groups are whole CTAs whose warps merge through shared memory when their
+    // merge rows fit beside the stages. Otherwise: single-warp groups when no
+    // segment can exceed 8 tiles (no cross-group merge of more than 8 pieces),
+    // else whole CTAs with the warps' merge rows in the workspace (a long
+    // segment would otherwise split into one piece per warp).
     const int group_bytes = v.nw * 2 * (pl.D + 4) * 4 * pl.slot_cols;
-    pl.gsz = (base + group_bytes <= kMaxSmem) ? v.nw : 1;
-    pl.smem = base + (pl.gsz > 1 ? group_bytes : 0);
+    const long long max_nt = (cap + v.tile - 1) / v.tile;
+    pl.gsz = v.nw;
+    if (base + group_bytes > kMaxSmem) {
+      if (max_nt <= 8)
+        pl.gsz = 1;
+      else
+        pl.wslot_global = true;
+    }
+    pl.smem = base + ((pl.gsz > 1 && !pl.wslot_global) ? group_bytes : 0);
     const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);   // two per group
-    pl.ws_bytes = slots * pl.slot_cols * (pl.D + 1) * sizeof(float);
+    pl.ws_bytes = group_slot_bytes(pl, slots);
+    if (pl.wslot_global) pl.ws_bytes += static_cast<size_t>(pl.grid) * group_bytes;
   } else {
     pl.smem = variant_smem_base(pl.variant, pl.dup, pl.D);
     const long long workers = static_cast<long long>(p->batch) * nseg * pl.ns;
@@ -1843,8 +1880,11 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   kp.scale_log2 = p->scale * kLog2e;
   if (pl.ns == 0) {
     float* ws = static_cast<float*>(p->workspace);
+    const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);
     kp.o_part = ws;
-    kp.lse_part = ws + static_cast<size_t>(2) * (pl.W / pl.gsz) * pl.slot_cols * pl.D;
+    kp.lse_part = ws + slots * pl.slot_cols * pl.D;
+    if (pl.wslot_global)
+      kp.wslots = ws + group_slot_bytes(pl, slots) / sizeof(float);
   } else if (p->o_partial && p->lse_partial) {
     kp.o_part = p->o_partial;
     kp.lse_part = p->lse_partial;

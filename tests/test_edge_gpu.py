@@ -106,3 +106,27 @@ def test_padded_cache_strides(pa, oracle, head_dim):
     bt = torch.randperm(nb, generator=g, device="cuda")[: b * 10].reshape(b, 10).int()
     _run_and_check(pa, oracle, q, k, v, bt, s, bs)
     _run_and_check(pa, oracle, q, k, v, bt, s, bs, num_splits=2)
+
+
+@pytest.mark.parametrize("head_dim,hq,hkv,variant", [(128, 32, 8, 3), (64, 64, 8, 8),
+                                                    (256, 16, 2, 9)])
+def test_long_segments_merge_rows_in_workspace(pa, oracle, head_dim, hq, hkv, variant):
+    """Variants whose warps' merge rows do not fit in shared memory beside the
+    stages, with segments far longer than 8 tiles: the CTA-level merge goes
+    through the workspace (same-length and per-row lengths, both checked)."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(head_dim + variant)
+    b, s, bs = 3, 20000, 16
+    lens = torch.randint(s // 2, s, (b,), generator=g, dtype=torch.int32)
+    nblk = (s + bs - 1) // bs
+    w = workloads.build("long_ws", b, hq, hkv, bs, torch.bfloat16, lens.cuda(), nblk, b * nblk,
+                        seed=variant, device="cuda", head_dim=head_dim)
+    for lengths in (lens.cuda(), s - 3):
+        ws = pa.DecodeWorkspace("cuda")
+        o, lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, lengths, bs,
+                                    return_lse=True, workspace=ws, kernel_variant=variant)
+        torch.cuda.synchronize()
+        assert ws.read_status() == 0
+        ro, rl = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, lengths, bs)
+        assert_o_close(o, ro, "O")
+        assert_lse_close(lse, rl, "LSE")
