@@ -2,10 +2,14 @@
 
     python compare_libs.py [--configs c1,c2,c3,c4,c5] [--iters 50]
     python compare_libs.py --head-dims 64,256 [--iters 50]
+    python compare_libs.py --long [--iters 50]
 
 ``--head-dims`` runs C2-sized MHA steps (B=32, S=1024, block 16, fp16, 537 MB
 of K/V) at other head dimensions instead of the five configurations (query
-heads chosen so the bytes match: 64 heads at D=64, 16 at D=256).
+heads chosen so the bytes match: 64 heads at D=64, 16 at D=256). ``--long``
+runs long-context shapes: one 131072-token sequence (MHA 8 heads fp16, and
+Hq 32 / Hkv 8 bf16), 8 sequences of 32768 tokens and 64 ragged sequences of
+1K-8K tokens (Hq 32 / Hkv 8 bf16), block 16.
 
 For each benchmark shape it times this operator, vLLM's
 ``paged_attention_v1`` / ``paged_attention_v2`` (the kernels the reference's
@@ -138,9 +142,25 @@ def main():
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--head-dims", default="", help="e.g. 64,256: C2-sized MHA at these D")
+    ap.add_argument("--long", action="store_true", help="long-context shapes")
     a = ap.parse_args()
     flush = _Flush()
-    if a.head_dims:
+    if a.long:
+        g = torch.Generator().manual_seed(7)
+        ragged = torch.randint(1024, 8193, (64,), generator=g, dtype=torch.int32)
+        bf16, f16 = torch.bfloat16, torch.float16
+        builders = [
+            ("b1_s131072_h8_mha_f16", lambda: workloads.build(
+                "b1_s131072_h8_mha_f16", 1, 8, 8, 16, f16, 131072, 8192, 8192, 1, "cuda")),
+            ("b1_s131072_hq32_hkv8_bf16", lambda: workloads.build(
+                "b1_s131072_hq32_hkv8_bf16", 1, 32, 8, 16, bf16, 131072, 8192, 8192, 2, "cuda")),
+            ("b8_s32768_hq32_hkv8_bf16", lambda: workloads.build(
+                "b8_s32768_hq32_hkv8_bf16", 8, 32, 8, 16, bf16, 32768, 2048, 16384, 3, "cuda")),
+            ("b64_ragged1k-8k_hq32_hkv8_bf16", lambda: workloads.build(
+                "b64_ragged1k-8k_hq32_hkv8_bf16", 64, 32, 8, 16, bf16, ragged.cuda(), 512,
+                64 * 512, 4, "cuda")),
+        ]
+    elif a.head_dims:
         heads = {64: 64, 128: 32, 256: 16}
         builders = [(f"c2size_d{d}", (lambda d=d: workloads.build(
             f"c2size_mha_d{d}_h{heads[d]}_s1024_bs16_f16", 32, heads[d], heads[d], 16,
