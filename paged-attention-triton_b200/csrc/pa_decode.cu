@@ -665,6 +665,39 @@ __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg
   if (lane == 0) atomicExch(p.counters + cid, 0);
 }
 
+// Cold paths, out of line so that the hot path's straight-line code does not
+// interleave with them (the short steps are bound by instruction fetch).
+
+// A barrier wait gave up: flag it and wait (bounded) for the `more` copies
+// still in flight on the other stages, so that none lands after the exit.
+template <int NS>
+__device__ __noinline__ void drain_after_timeout(unsigned* status, uint32_t bar0, int st,
+                                                 uint32_t phase, int more) {
+  if (status) atomicOr(status, PA_STATUS_TIMEOUT);
+  for (int k = 1; k < NS && k <= more; ++k) {
+    const int s2 = (st + k) % NS;
+    mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1);
+  }
+}
+
+// Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
+template <int D, bool kCum>
+__device__ __noinline__ void zero_length_rows(int B, int Hq, char* out, long long o_sb,
+                                              long long o_sh, float* lse, const int* seq_lens,
+                                              int seq_len) {
+  for (int b = blockIdx.x; b < B; b += gridDim.x) {
+    // negative lengths count as 0 (and are flagged by the prefix-sum pass)
+    const int S = kCum ? max(0, __ldg(seq_lens + b)) : seq_len;
+    if (S != 0) continue;
+    for (int idx = threadIdx.x; idx < Hq * (D / 8); idx += blockDim.x) {
+      const int h = idx / (D / 8), c = idx % (D / 8);
+      *reinterpret_cast<uint4*>(out + b * o_sb + h * o_sh + c * 16) = make_uint4(0, 0, 0, 0);
+    }
+    if (lse)
+      for (int h = threadIdx.x; h < Hq; h += blockDim.x) lse[b * Hq + h] = kSentinel;
+  }
+}
+
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
@@ -765,19 +798,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     __syncthreads();
   }
 
-  // Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
-  if (!kSplit && p.zero_rows) {
-    for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-      if (row_len<kCum>(p, b) != 0) continue;
-      for (int idx = threadIdx.x; idx < p.Hq * (D / 8); idx += blockDim.x) {
-        const int h = idx / (D / 8), c = idx % (D / 8);
-        *reinterpret_cast<uint4*>(p.out + b * p.o_sb + h * p.o_sh + c * 16) =
-            make_uint4(0, 0, 0, 0);
-      }
-      if (p.lse)
-        for (int h = threadIdx.x; h < p.Hq; h += blockDim.x) p.lse[b * p.Hq + h] = kSentinel;
-    }
-  }
+  if (!kSplit && p.zero_rows)
+    zero_length_rows<D, kCum>(p.B, p.Hq, p.out, p.o_sb, p.o_sh, p.lse, p.seq_lens, p.seq_len);
 
   const int G = p.G;
   const int spt_mask = (1 << p.lspt) - 1;
@@ -966,12 +988,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     const uint32_t sq = sk + 2 * C::kKV;
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
-      flag(p, PA_STATUS_TIMEOUT);
-      // drain the copies still in flight for the other stages (bounded), then leave
-      for (int k = 1; k < NS && i + k < issued; ++k) {
-        const int s2 = (st + k) % NS;
-        mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1);
-      }
+      drain_after_timeout<NS>(p.status, bar0, st, phase, issued - i - 1);
       return;
     }
     phase ^= 1u << st;
