@@ -123,6 +123,7 @@ struct KParams {
   FastDiv div_bs;           // by bs (pages that are not a power of two)
   FastDiv div_ng;           // by the number of groups (P with per-row lengths)
   float* wslots;            // warps' merge rows in global memory (null: shared memory)
+  int post_merge;           // 1: segments that cross groups merge in merge_segments_kernel
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -648,10 +649,12 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, i
 }
 
 // Publishes the group's piece (already written to its global slot) and merges
-// the segment if this group arrived last.
+// the segment if this group arrived last; with post_merge the slot is only
+// written, for merge_segments_kernel.
 template <typename T, int D>
 __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg, int b, int kvh,
                                               int qc, int gc, int seg_lo, int seg_hi, int lane) {
+  if (p.post_merge) return;   // the merge kernel that follows reads the slots
   __threadfence();
   __syncwarp();
   const int n = (seg_hi - 1) / rg.P - seg_lo / rg.P + 1;
@@ -1314,6 +1317,209 @@ __global__ void __launch_bounds__(256) cache_append_kernel(const AppendParams a)
 }
 
 // ----------------------------------------------------------------------------
+// Cross-group merge pass (balanced schedule)
+// ----------------------------------------------------------------------------
+// When few segments each span many groups, every group finishes at about the
+// same time and the in-kernel merge (the last group's one warp walking gc
+// columns x n pieces, an L2 round trip per column and per 8 pieces) is the
+// step's tail. This kernel follows the decode kernel in the stream instead
+// (programmatic dependent launch): one CTA per segment that crosses a group
+// boundary, its eight warps split over the segment's columns and, for fewer
+// columns, over its pieces; each lane keeps 64 floats of pieces in flight.
+// Same arithmetic as merge_rows (split_kv_kernel.py:101-122): pieces with
+// LSE <= -1e29 are skipped and the sum is clamped at 1e-20.
+struct MergeParams {
+  const float* o_part;      // group slots [2 * groups][slot_cols][D]
+  const float* lse_part;    // [2 * groups][slot_cols]
+  char* out;
+  long long o_sb, o_sh;     // bytes
+  float* lse;
+  const int* seq_lens;      // per-row lengths (kCum), clamped to [0, cap]
+  int cap;
+  int B, Hkv, G, QC, slot_cols;
+  int tile;                 // tokens per unit
+  int ngroups, gsz;
+  int U, P, nt_u, per_row;  // same-length rows; P: units per group
+  int by_segment;           // 1: block x is a segment, 0: block x + 1 is a group boundary
+};
+
+template <typename T, int D, bool kCum>
+__global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m) {
+  constexpr int N = HD<D>::kLaneF;
+  constexpr int kRows = 64 / N;   // pieces in flight per lane
+  __shared__ __align__(16) float s_acc[8][D];
+  __shared__ float s_ml[8][2];
+  __shared__ int s_cum[kCum ? kCumMax + 1 : 1];
+  __shared__ int s_tot[8];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // The decode kernel's partials are complete and visible after the wait.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  const int nseg = m.Hkv * m.QC;   // segments per row
+  int U = m.U, P = m.P;
+  if constexpr (kCum) {
+    // Per-row unit prefix sums, formed as the decode kernel forms them.
+    const int chunk = (m.B + 255) / 256;
+    const int lo = min(m.B, static_cast<int>(threadIdx.x) * chunk);
+    const int hi = min(m.B, lo + chunk);
+    int local = 0;
+    for (int b = lo; b < hi; ++b) {
+      const int S = min(max(__ldg(m.seq_lens + b), 0), m.cap);
+      local += nseg * ((S + m.tile - 1) / m.tile);
+    }
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_tot[warp] = incl;
+    __syncthreads();
+    int run = incl - local;
+    for (int k = 0; k < warp; ++k) run += s_tot[k];
+    for (int b = lo; b < hi; ++b) {
+      s_cum[b] = run;
+      const int S = min(max(__ldg(m.seq_lens + b), 0), m.cap);
+      run += nseg * ((S + m.tile - 1) / m.tile);
+    }
+    if (threadIdx.x == 255) s_cum[m.B] = run;
+    __syncthreads();
+    U = s_cum[m.B];
+    P = max((U + m.ngroups - 1) / m.ngroups, m.gsz);
+  }
+
+  // The segment: units [seg_lo, seg_lo + nt) of row b, segment index seg.
+  int b, seg, seg_lo, nt;
+  if (m.by_segment) {
+    b = blockIdx.x / nseg;
+    seg = blockIdx.x - b * nseg;
+    if constexpr (kCum) {
+      const int S = min(max(__ldg(m.seq_lens + b), 0), m.cap);
+      nt = (S + m.tile - 1) / m.tile;
+      seg_lo = s_cum[b] + seg * nt;
+    } else {
+      nt = m.nt_u;
+      seg_lo = b * m.per_row + seg * nt;
+    }
+    if (nt == 0 || seg_lo / P == (seg_lo + nt - 1) / P) return;   // inside one group
+  } else {
+    const long long u64 = static_cast<long long>(blockIdx.x + 1) * P;
+    if (u64 >= U) return;
+    const int u = static_cast<int>(u64);
+    int row_base;
+    if constexpr (kCum) {
+      b = find_row(s_cum, m.B, u);
+      row_base = s_cum[b];
+      const int S = min(max(__ldg(m.seq_lens + b), 0), m.cap);
+      nt = (S + m.tile - 1) / m.tile;
+    } else {
+      b = u / m.per_row;
+      row_base = b * m.per_row;
+      nt = m.nt_u;
+    }
+    seg = (u - row_base) / nt;
+    seg_lo = row_base + seg * nt;
+    // Only the segment's first crossing merges it.
+    if (seg_lo == u || seg_lo / P != static_cast<int>(blockIdx.x)) return;
+  }
+  const int seg_hi = seg_lo + nt;
+  const int g_first = seg_lo / P;
+  const int n = (seg_hi - 1) / P - g_first + 1;
+  const int kvh = seg / m.QC;
+  const int qc = seg - kvh * m.QC;
+  const int gc = min(8, m.G - qc * 8);
+  const int wpc = 8 / gc;           // warps per column
+  const int j = warp / wpc;         // column
+  const int r = warp - j * wpc;     // this warp's pieces: r, r + wpc, ...
+
+  float mx = kValidLse, sum = 0.f;
+  RowV<N> acc;
+#pragma unroll
+  for (int i = 0; i < N; ++i) acc.f[i] = 0.f;
+  if (j < gc) {
+    for (int k0 = r; k0 < n; k0 += kRows * wpc) {
+      float l[kRows];
+      RowV<N> v[kRows];
+#pragma unroll
+      for (int t = 0; t < kRows; ++t) {
+        const int k = k0 + t * wpc;
+        if (k < n) {
+          const int g = g_first + k;
+          const long long sl = 2ll * g + (max(seg_lo, g * P) == g * P ? 0 : 1);
+          l[t] = __ldcg(m.lse_part + sl * m.slot_cols + j);
+          v[t] = load_row<true, N>(m.o_part + (sl * m.slot_cols + j) * D, lane);
+        } else {
+          l[t] = kSentinel;
+#pragma unroll
+          for (int i = 0; i < N; ++i) v[t].f[i] = 0.f;
+        }
+      }
+      float bm = mx;
+#pragma unroll
+      for (int t = 0; t < kRows; ++t)
+        if (l[t] > kValidLse) bm = fmaxf(bm, l[t]);
+      const float f = exp2f((mx - bm) * kLog2e);
+      sum *= f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) acc.f[i] *= f;
+#pragma unroll
+      for (int t = 0; t < kRows; ++t) {
+        const float wgt = (l[t] > kValidLse) ? exp2f((l[t] - bm) * kLog2e) : 0.f;
+        sum += wgt;
+#pragma unroll
+        for (int i = 0; i < N; ++i) acc.f[i] = fmaf(wgt, v[t].f[i], acc.f[i]);
+      }
+      mx = bm;
+    }
+  }
+  if (wpc > 1) {   // the column's warps meet in shared memory
+    if (j < gc) {
+      store_row(&s_acc[warp][0], lane, acc);
+      if (lane == 0) {
+        s_ml[warp][0] = mx;
+        s_ml[warp][1] = sum;
+      }
+    }
+    __syncthreads();
+    if (j < gc && r == 0) {
+      float M = kValidLse;
+      for (int i = 0; i < wpc; ++i) M = fmaxf(M, s_ml[warp + i][0]);
+      sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) acc.f[i] = 0.f;
+      for (int w2 = 0; w2 < wpc; ++w2) {
+        const float f = exp2f((s_ml[warp + w2][0] - M) * kLog2e);
+        sum = fmaf(s_ml[warp + w2][1], f, sum);
+        const RowV<N> a2 = load_row<false, N>(&s_acc[warp + w2][0], lane);
+#pragma unroll
+        for (int i = 0; i < N; ++i) acc.f[i] = fmaf(f, a2.f[i], acc.f[i]);
+      }
+      mx = M;
+    }
+  }
+  if (j >= gc || r != 0) return;
+  const float inv = 1.f / fmaxf(sum, 1e-20f);
+  const int hq = kvh * m.G + qc * 8 + j;
+  char* dst = m.out + b * m.o_sb + hq * m.o_sh + lane * N * 2;
+  uint32_t w[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i)
+    w[i] = pack16(Mma<T>::from_float(acc.f[2 * i] * inv),
+                  Mma<T>::from_float(acc.f[2 * i + 1] * inv));
+  if constexpr (N == 2) {
+    *reinterpret_cast<uint32_t*>(dst) = w[0];
+  } else if constexpr (N == 4) {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  if (lane == 0 && m.lse) m.lse[b * m.G * m.Hkv + hq] = sum > 0.f ? mx + logf(sum) : kSentinel;
+}
+
+// ----------------------------------------------------------------------------
 // Bandwidth probes (replace measure_peak_bw.py:15-21's Triton copy kernel)
 // ----------------------------------------------------------------------------
 __global__ void __launch_bounds__(512) stream_copy_kernel(const uint4* __restrict__ src,
@@ -1805,6 +2011,65 @@ static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   return launch_one<T, kDup, 32, 4, 3, 128>(pl, mk, mv, kp, stream, dev);
 }
 
+template <typename T, int D, bool kCum>
+static cudaError_t launch_merge_kernel(const MergeParams& m, int grid, cudaStream_t stream) {
+  // Dependent launch: the grid may be scheduled while the decode kernel runs;
+  // griddepcontrol.wait orders its reads after that kernel's completion.
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_segments_kernel<T, D, kCum>, m);
+}
+
+template <typename T>
+static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, int grid,
+                                cudaStream_t stream) {
+  if (D == 64)
+    return cum ? launch_merge_kernel<T, 64, true>(m, grid, stream)
+               : launch_merge_kernel<T, 64, false>(m, grid, stream);
+  if (D == 256)
+    return cum ? launch_merge_kernel<T, 256, true>(m, grid, stream)
+               : launch_merge_kernel<T, 256, false>(m, grid, stream);
+  return cum ? launch_merge_kernel<T, 128, true>(m, grid, stream)
+             : launch_merge_kernel<T, 128, false>(m, grid, stream);
+}
+
+// Whether the segments that cross group boundaries merge in
+// merge_segments_kernel rather than by the last group's warp inside the
+// decode kernel, and that kernel's grid. The pass costs a dependent launch
+// (about 5 us on B200); the in-kernel merge costs an L2 round trip per column
+// and per 8 pieces on the step's tail, which is exposed when few long segments
+// finish together. From B200 sweeps: the pass wins for query-head groups
+// (two or more columns) and for single columns over more than 8 pieces, and
+// loses for single-warp groups (short segments, merged in parallel by many
+// warps) and for per-row lengths with more segments than groups.
+static bool want_post_merge(const pa_decode_params* p, const Plan& pl, const KParams& kp,
+                            int& grid, int& by_segment) {
+  if (pl.ns != 0 || pl.gsz == 1) return false;
+  const int ngroups = pl.W / pl.gsz;
+  if (ngroups < 2) return false;
+  const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
+  if (!pl.use_cum) {
+    // Segments start at multiples of nt_u: none crosses a group boundary when
+    // P is one, or when one group holds every unit.
+    if (kp.nt_u == 0 || kp.U <= kp.P || kp.P % kp.nt_u == 0) return false;
+    const int n_max = (kp.nt_u + kp.P - 2) / kp.P + 1;   // groups a segment may span
+    if (pl.slot_cols < 2 && n_max <= 8) return false;
+  } else if (nseg_total * (pl.slot_cols < 2 ? 8 : 1) >= ngroups) {
+    return false;   // lengths are on the device: judged by segments per group
+  }
+  by_segment = nseg_total <= ngroups - 1 ? 1 : 0;
+  grid = by_segment ? static_cast<int>(nseg_total) : ngroups - 1;
+  return true;
+}
+
 }  // namespace pa
 
 using namespace pa;
@@ -1957,6 +2222,9 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
                         p->v_stride_head, kp.R))
     return PA_ERR_ARG;
 
+  int merge_grid = 0, by_segment = 0;
+  kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment) ? 1 : 0;
+
   cudaError_t e;
   if (p->dtype == PA_F16)
     e = pl.dup ? launch<__half, true>(pl, mk, mv, kp, stream, dev)
@@ -1964,6 +2232,33 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   else
     e = pl.dup ? launch<__nv_bfloat16, true>(pl, mk, mv, kp, stream, dev)
                : launch<__nv_bfloat16, false>(pl, mk, mv, kp, stream, dev);
+  if (e == cudaSuccess && kp.post_merge) {
+    MergeParams m;
+    memset(&m, 0, sizeof(m));
+    m.o_part = kp.o_part;
+    m.lse_part = kp.lse_part;
+    m.out = kp.out;
+    m.o_sb = kp.o_sb;
+    m.o_sh = kp.o_sh;
+    m.lse = kp.lse;
+    m.seq_lens = kp.seq_lens;
+    m.cap = kp.max_blocks * kp.bs;
+    m.B = kp.B;
+    m.Hkv = kp.Hkv;
+    m.G = kp.G;
+    m.QC = kp.QC;
+    m.slot_cols = kp.slot_cols;
+    m.tile = tile;
+    m.ngroups = pl.W / pl.gsz;
+    m.gsz = pl.gsz;
+    m.U = kp.U;
+    m.P = kp.P;
+    m.nt_u = kp.nt_u;
+    m.per_row = kp.per_row;
+    m.by_segment = by_segment;
+    e = p->dtype == PA_F16 ? launch_merge<__half>(m, pl.D, pl.use_cum, merge_grid, stream)
+                           : launch_merge<__nv_bfloat16>(m, pl.D, pl.use_cum, merge_grid, stream);
+  }
   return e == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

@@ -108,6 +108,41 @@ def test_padded_cache_strides(pa, oracle, head_dim):
     _run_and_check(pa, oracle, q, k, v, bt, s, bs, num_splits=2)
 
 
+@pytest.mark.parametrize("head_dim,hq,hkv,b,s,per_row", [
+    (128, 64, 8, 1, 8192, False), (128, 64, 8, 1, 8192, True), (128, 32, 4, 1, 32768, False),
+    (128, 32, 8, 4, 2048, True), (128, 24, 2, 2, 9000, False), (128, 8, 8, 1, 131072, False),
+    (64, 64, 8, 1, 16384, False), (64, 16, 2, 3, 5000, True), (256, 16, 2, 1, 12000, False),
+    (256, 16, 16, 1, 16384, True)])
+def test_few_long_segments_merge_pass(pa, oracle, head_dim, hq, hkv, b, s, per_row):
+    """Few segments, each spread over many CTAs: the pieces merge in the
+    separate merge kernel that follows the decode kernel (one CTA per crossing
+    segment, its warps over the columns and pieces), for query-head groups of
+    2-8 columns and partial column chunks (G = 12), single columns spanning
+    more than 8 groups, same-length and per-row lengths, D = 64, 128, 256."""
+    from paged_attention import workloads
+    bs = 16
+    nblk = (s + bs - 1) // bs
+    w = workloads.build("merge_pass", b, hq, hkv, bs, torch.bfloat16, s, nblk, b * nblk,
+                        seed=hq + s, device="cuda", head_dim=head_dim)
+    if per_row:
+        lens = torch.tensor([s - 7 * i for i in range(b)], dtype=torch.int32, device="cuda")
+    else:
+        lens = s
+    ws = pa.DecodeWorkspace("cuda")
+    for rep in range(2):   # the second call reuses the workspace as left by the first
+        o, lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs,
+                                    return_lse=True, workspace=ws)
+        torch.cuda.synchronize()
+        assert ws.read_status() == 0
+    ro, rl = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs)
+    assert_o_close(o, ro, "O")
+    assert_lse_close(lse, rl, "LSE")
+    # the split schedule on the same inputs (no merge pass) agrees too
+    o2 = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs, 7)
+    torch.cuda.synchronize()
+    assert_o_close(o2, ro, "O split")
+
+
 @pytest.mark.parametrize("head_dim,hq,hkv,variant", [(128, 32, 8, 3), (64, 64, 8, 8),
                                                     (256, 16, 2, 9)])
 def test_long_segments_merge_rows_in_workspace(pa, oracle, head_dim, hq, hkv, variant):
