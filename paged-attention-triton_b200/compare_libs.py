@@ -3,13 +3,17 @@
     python compare_libs.py [--configs c1,c2,c3,c4,c5] [--iters 50]
     python compare_libs.py --head-dims 64,256 [--iters 50]
     python compare_libs.py --long [--iters 50]
+    python compare_libs.py --small-batch [--iters 50]
 
 ``--head-dims`` runs C2-sized MHA steps (B=32, S=1024, block 16, fp16, 537 MB
 of K/V) at other head dimensions instead of the five configurations (query
 heads chosen so the bytes match: 64 heads at D=64, 16 at D=256). ``--long``
 runs long-context shapes: one 131072-token sequence (MHA 8 heads fp16, and
 Hq 32 / Hkv 8 bf16), 8 sequences of 32768 tokens and 64 ragged sequences of
-1K-8K tokens (Hq 32 / Hkv 8 bf16), block 16.
+1K-8K tokens (Hq 32 / Hkv 8 bf16), block 16. ``--small-batch`` runs
+grouped-query shapes with few sequences (1-64 rows of 512-32768 tokens,
+Hq 32 or 64 over Hkv 4 or 8, bf16, block 16), where few long segments spread
+over many CTAs and the cross-CTA merge is the step's tail.
 
 For each benchmark shape it times this operator, vLLM's
 ``paged_attention_v1`` / ``paged_attention_v2`` (the kernels the reference's
@@ -143,6 +147,7 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--head-dims", default="", help="e.g. 64,256: C2-sized MHA at these D")
     ap.add_argument("--long", action="store_true", help="long-context shapes")
+    ap.add_argument("--small-batch", action="store_true", help="few-sequence GQA shapes")
     a = ap.parse_args()
     flush = _Flush()
     if a.long:
@@ -160,6 +165,14 @@ def main():
                 "b64_ragged1k-8k_hq32_hkv8_bf16", 64, 32, 8, 16, bf16, ragged.cuda(), 512,
                 64 * 512, 4, "cuda")),
         ]
+    elif a.small_batch:
+        shapes = [(1, 1024, 32, 8), (1, 4096, 32, 8), (4, 2048, 32, 8), (16, 1024, 32, 8),
+                  (64, 512, 32, 8), (1, 8192, 64, 8), (8, 4096, 64, 8), (1, 32768, 32, 4)]
+        builders = [(f"b{b}_s{s}_hq{hq}_hkv{hkv}_bf16", (lambda b=b, s=s, hq=hq, hkv=hkv:
+                     workloads.build(f"b{b}_s{s}_hq{hq}_hkv{hkv}_bf16", b, hq, hkv, 16,
+                                     torch.bfloat16, s, (s + 15) // 16, b * ((s + 15) // 16),
+                                     1, "cuda")))
+                    for b, s, hq, hkv in shapes]
     elif a.head_dims:
         heads = {64: 64, 128: 32, 256: 16}
         builders = [(f"c2size_d{d}", (lambda d=d: workloads.build(

@@ -1341,6 +1341,7 @@ struct MergeParams {
   int ngroups, gsz;
   int U, P, nt_u, per_row;  // same-length rows; P: units per group
   int by_segment;           // 1: block x is a segment, 0: block x + 1 is a group boundary
+  int col_split;            // 1: block y is one query column (segments of many pieces)
 };
 
 template <typename T, int D, bool kCum>
@@ -1430,16 +1431,23 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m
   const int n = (seg_hi - 1) / P - g_first + 1;
   const int kvh = seg / m.QC;
   const int qc = seg - kvh * m.QC;
-  const int gc = min(8, m.G - qc * 8);
+  int gc = min(8, m.G - qc * 8);
+  int j0 = 0;                       // first column of this CTA
+  if (m.col_split) {
+    j0 = blockIdx.y;
+    if (j0 >= gc) return;
+    gc = 1;                         // columns of this CTA
+  }
   const int wpc = 8 / gc;           // warps per column
-  const int j = warp / wpc;         // column
-  const int r = warp - j * wpc;     // this warp's pieces: r, r + wpc, ...
+  const int jl = warp / wpc;        // column of this warp, within the CTA's
+  const int r = warp - jl * wpc;    // this warp's pieces: r, r + wpc, ...
+  const int j = j0 + jl;
 
   float mx = kValidLse, sum = 0.f;
   RowV<N> acc;
 #pragma unroll
   for (int i = 0; i < N; ++i) acc.f[i] = 0.f;
-  if (j < gc) {
+  if (jl < gc) {
     for (int k0 = r; k0 < n; k0 += kRows * wpc) {
       float l[kRows];
       RowV<N> v[kRows];
@@ -1476,7 +1484,7 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m
     }
   }
   if (wpc > 1) {   // the column's warps meet in shared memory
-    if (j < gc) {
+    if (jl < gc) {
       store_row(&s_acc[warp][0], lane, acc);
       if (lane == 0) {
         s_ml[warp][0] = mx;
@@ -1484,7 +1492,7 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m
       }
     }
     __syncthreads();
-    if (j < gc && r == 0) {
+    if (jl < gc && r == 0) {
       float M = kValidLse;
       for (int i = 0; i < wpc; ++i) M = fmaxf(M, s_ml[warp + i][0]);
       sum = 0.f;
@@ -1500,7 +1508,7 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m
       mx = M;
     }
   }
-  if (j >= gc || r != 0) return;
+  if (jl >= gc || r != 0) return;
   const float inv = 1.f / fmaxf(sum, 1e-20f);
   const int hq = kvh * m.G + qc * 8 + j;
   char* dst = m.out + b * m.o_sb + hq * m.o_sh + lane * N * 2;
@@ -1647,6 +1655,7 @@ struct Plan {
   int variant = 1;   // 1-based index into kVariants
   bool use_cum = false;
   bool wslot_global = false;   // balanced: warps' merge rows in the workspace
+  bool long_pieces = false;    // balanced: single-warp groups over long segments
   int slot_cols = 1;
   int gsz = 1;             // balanced: warps per merge group
   int smem = 0;            // dynamic shared memory of the launch
@@ -1785,17 +1794,27 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     const int base = variant_smem_base(pl.variant, pl.dup, pl.D);
     // Groups are whole CTAs whose warps merge through shared memory when their
     // merge rows fit beside the stages. Otherwise: single-warp groups when no
-    // segment can exceed 8 tiles (no cross-group merge of more than 8 pieces),
-    // else whole CTAs with the warps' merge rows in the workspace (a long
-    // segment would otherwise split into one piece per warp).
+    // segment can exceed 8 tiles (no cross-group merge of more than 8 pieces)
+    // or when there are no more segments than CTAs (their pieces merge in the
+    // merge pass), else whole CTAs with the warps' merge rows in the workspace
+    // (a long segment would otherwise split into one piece per warp, merged by
+    // one warp).
     const int group_bytes = v.nw * 2 * (pl.D + 4) * 4 * pl.slot_cols;
     const long long max_nt = (cap + v.tile - 1) / v.tile;
     pl.gsz = v.nw;
     if (base + group_bytes > kMaxSmem) {
-      if (max_nt <= 8)
+      if (max_nt <= 8) {
         pl.gsz = 1;
-      else
+      } else if (static_cast<long long>(p->batch) * nseg <= pl.grid) {
+        // No more segments than CTAs: each spans CTAs, and one warp per CTA
+        // would merge its warps' rows column after column from the workspace
+        // (an L2 round trip each). Single-warp groups instead, whose pieces
+        // all merge in the merge pass after the decode kernel.
+        pl.gsz = 1;
+        pl.long_pieces = true;
+      } else {
         pl.wslot_global = true;
+      }
     }
     pl.smem = base + ((pl.gsz > 1 && !pl.wslot_global) ? group_bytes : 0);
     const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);   // two per group
@@ -2012,14 +2031,14 @@ static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorM
 }
 
 template <typename T, int D, bool kCum>
-static cudaError_t launch_merge_kernel(const MergeParams& m, int grid, cudaStream_t stream) {
+static cudaError_t launch_merge_kernel(const MergeParams& m, dim3 grid, cudaStream_t stream) {
   // Dependent launch: the grid may be scheduled while the decode kernel runs;
   // griddepcontrol.wait orders its reads after that kernel's completion.
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
@@ -2029,7 +2048,7 @@ static cudaError_t launch_merge_kernel(const MergeParams& m, int grid, cudaStrea
 }
 
 template <typename T>
-static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, int grid,
+static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, dim3 grid,
                                 cudaStream_t stream) {
   if (D == 64)
     return cum ? launch_merge_kernel<T, 64, true>(m, grid, stream)
@@ -2050,23 +2069,30 @@ static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, int grid,
 // (two or more columns) and for single columns over more than 8 pieces, and
 // loses for single-warp groups (short segments, merged in parallel by many
 // warps) and for per-row lengths with more segments than groups.
+// Single-warp groups over long segments (pl.long_pieces) always take the pass.
 static bool want_post_merge(const pa_decode_params* p, const Plan& pl, const KParams& kp,
-                            int& grid, int& by_segment) {
-  if (pl.ns != 0 || pl.gsz == 1) return false;
+                            dim3& grid, int& by_segment, int& col_split) {
+  if (pl.ns != 0 || (pl.gsz == 1 && !pl.long_pieces)) return false;
   const int ngroups = pl.W / pl.gsz;
   if (ngroups < 2) return false;
   const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
+  long long pieces;   // groups a segment may span
   if (!pl.use_cum) {
     // Segments start at multiples of nt_u: none crosses a group boundary when
     // P is one, or when one group holds every unit.
     if (kp.nt_u == 0 || kp.U <= kp.P || kp.P % kp.nt_u == 0) return false;
-    const int n_max = (kp.nt_u + kp.P - 2) / kp.P + 1;   // groups a segment may span
-    if (pl.slot_cols < 2 && n_max <= 8) return false;
-  } else if (nseg_total * (pl.slot_cols < 2 ? 8 : 1) >= ngroups) {
-    return false;   // lengths are on the device: judged by segments per group
+    pieces = (kp.nt_u + kp.P - 2) / kp.P + 1;
+    if (!pl.long_pieces && pl.slot_cols < 2 && pieces <= 8) return false;
+  } else {
+    // lengths are on the device: judged by segments per group
+    if (!pl.long_pieces && nseg_total * (pl.slot_cols < 2 ? 8 : 1) >= ngroups) return false;
+    pieces = ngroups / std::max(1ll, nseg_total) + 1;
   }
   by_segment = nseg_total <= ngroups - 1 ? 1 : 0;
-  grid = by_segment ? static_cast<int>(nseg_total) : ngroups - 1;
+  // More than 32 pieces a column: one column per CTA, its eight warps over the pieces.
+  col_split = (pieces > 32 && pl.slot_cols > 1) ? 1 : 0;
+  grid = dim3(by_segment ? static_cast<unsigned>(nseg_total) : static_cast<unsigned>(ngroups - 1),
+              col_split ? static_cast<unsigned>(pl.slot_cols) : 1u);
   return true;
 }
 
@@ -2222,8 +2248,9 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
                         p->v_stride_head, kp.R))
     return PA_ERR_ARG;
 
-  int merge_grid = 0, by_segment = 0;
-  kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment) ? 1 : 0;
+  dim3 merge_grid(1);
+  int by_segment = 0, col_split = 0;
+  kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment, col_split) ? 1 : 0;
 
   cudaError_t e;
   if (p->dtype == PA_F16)
@@ -2256,6 +2283,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
     m.nt_u = kp.nt_u;
     m.per_row = kp.per_row;
     m.by_segment = by_segment;
+    m.col_split = col_split;
     e = p->dtype == PA_F16 ? launch_merge<__half>(m, pl.D, pl.use_cum, merge_grid, stream)
                            : launch_merge<__nv_bfloat16>(m, pl.D, pl.use_cum, merge_grid, stream);
   }
