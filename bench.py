@@ -19,17 +19,35 @@ buffer and then reading another 512 MB buffer (so no dirty flush lines are left
 in L2) and each step has its own event pair. Per-step, L2-flushed timings are
 reported beside the headline either way.
 
-Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): weak scaling by
-KV head -- rank r holds its own 32-KV-head shard (own seeded pool and block
-table) of a 32N-head cache and decodes it independently; no collective touches
-the data path. Timing is the max over ranks; after timing, the outputs are
-all-gathered over NCCL and rank 0 checks sampled rows of every shard against
-the oracle.
+Beside the headline the JSON line carries:
+
+* ``c5_sharded`` (every N): the 70B-class grouped-query step (B=256, Hq 64 /
+  Hkv 8, log-uniform lengths 512-32768, bf16) sharded by KV head -- rank r
+  holds KV heads ``[r*8/N, (r+1)*8/N)``, their query heads and its own seeded
+  page pool, and decodes them independently (strong scaling: the total work is
+  fixed). Per-rank times are the max over ranks; the outputs are all-gathered
+  over NCCL after timing and sampled rows of every shard are checked against
+  the oracle.
+* ``per_config`` (N=1): the three short steps C1 (B1 S128 MHA fp16), C3 (B1
+  S4096 page 128 bf16) and C4 (B128 ragged GQA-4 bf16), each L2-flushed per
+  step (eager and graph replay), back to back over rotating copies of the
+  inputs (distinct seeded workloads whose bytes read per step add up to at
+  least twice the L2, so every step reads from HBM without a flush between
+  steps), and as back-to-back graph replays of one input (the reference's
+  Layer-3 latency method), with fractions of the measured HBM peak.
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): the headline is
+weak scaling by KV head -- rank r holds its own 32-KV-head shard (own seeded
+pool and block table) of a 32N-head cache and decodes it independently; no
+collective touches the data path. Timing is the max over ranks; after timing,
+the outputs are all-gathered over NCCL and rank 0 checks sampled rows of every
+shard against the oracle.
 
 ``--impl reference`` times the reference algorithm's CPU path (the FP32
 gather + softmax attention of the reference's ``tests/correctness.py:17-20``,
 restated in ``oracle/``) on the host cores, on a bounded sample of the same
-workload; under torchrun only rank 0 runs it.
+workload, with the same per-row routine as the b200 arm's ``cpu_baseline``;
+under torchrun only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -195,12 +213,36 @@ def max_over_ranks(values, dist, device):
     return t.tolist()
 
 
+def oracle_rows(w, rows):
+    """The oracle's O for rows ``rows`` of workload ``w`` (FP32, CPU), computed
+    on a compact copy of just those rows' pages: the pages are gathered on
+    ``w``'s device, so an 8 GB cache never crosses to the host."""
+    import oracle
+    lens = w.seq_list()
+    outs = []
+    for b in rows:
+        s_len = lens[b]
+        nblk = max(1, (s_len + w.block_size - 1) // w.block_size)
+        phys = w.block_table[b, :nblk].long()
+        kc = w.k_cache[phys].cpu()
+        vc = w.v_cache[phys].cpu()
+        bt = torch.arange(nblk, dtype=torch.int32).reshape(1, nblk)
+        ro, _ = oracle.decode_reference(w.q[b:b + 1], kc, vc, bt, [s_len], w.block_size)
+        outs.append(ro[0])
+    return torch.stack(outs)
+
+
+def rows_match(got_rows, ref_rows):
+    """The O tolerance of the parity contract: |got - ref| <= 2e-3 + 1e-2 |ref|."""
+    got = got_rows.float().cpu()
+    return bool(((got - ref_rows).abs() <= 2e-3 + 1e-2 * ref_rows.abs()).all())
+
+
 def gather_and_verify(out, local_ok, config, rank, world, dist, device, batch=None,
                       rows=None):
     """All-gather every rank's output; rank 0 rebuilds each shard's inputs from
     its seed and checks sampled rows against the oracle. Returns the verdict,
     agreed by all ranks (all_reduce MIN)."""
-    import oracle
     gathered = [torch.empty_like(out) for _ in range(world)]
     dist.all_gather(gathered, out)
     ok = bool(local_ok)
@@ -208,22 +250,93 @@ def gather_and_verify(out, local_ok, config, rank, world, dist, device, batch=No
         for r in range(world):
             wr = build_shard(config, r, world, device, batch=batch)
             sel = rows if rows is not None else [0, wr.batch - 1]
-            ro, _ = oracle.decode_reference(wr.q, wr.k_cache, wr.v_cache, wr.block_table,
-                                            wr.seq_len, wr.block_size, batch_indices=sel)
-            got = gathered[r].float().cpu()[sel]
-            ref = ro[sel]
-            ok &= bool(((got - ref).abs() <= 2e-3 + 1e-2 * ref.abs()).all())
+            ok &= rows_match(gathered[r][sel], oracle_rows(wr, sel))
             del wr
     flag = torch.tensor([1 if ok else 0], device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     return bool(flag.item())
 
 
+def workload_config(w, world, nbytes):
+    """The ``config`` object of a JSON line: the same for both arms."""
+    back_to_back = nbytes > 2 * L2_BYTES
+    return {
+        "workload": w.name,
+        "batch": w.batch, "num_heads": w.num_heads, "num_kv_heads": w.num_kv_heads,
+        "head_dim": w.q.shape[-1], "block_size": w.block_size,
+        "seq_len": w.seq_len if isinstance(w.seq_len, int) else "per-row",
+        "kv_bytes_per_rank": nbytes,
+        "l2": (f"inputs {nbytes / 1e6:.0f} MB per rank > 2x L2 (126 MB): the K steps run back "
+               "to back between one event pair, each streaming its inputs from HBM "
+               "(per-step-event timings with L2 flushed under us_per_step)"
+               if back_to_back else
+               "flushed before every step: 512 MB write, then 512 MB read (no dirty lines left)"),
+        "schedule": "token-balanced persistent",
+        "parallelism": (f"kv-head shards x{world}" if world > 1 else "single GPU"),
+    }
+
+
+# ----------------------------------------------------------------------------- timing
+class Timer:
+    """CUDA-event timing on one stream, with a barrier (all ranks, then the
+    device) on both sides of every timed region."""
+
+    def __init__(self, stream, dev, dist, flusher):
+        self.stream, self.dev, self.dist, self.flusher = stream, dev, dist, flusher
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def per_step(self, fn, steps, flush=True):
+        """Per-step events around every step (L2 flushed before each)."""
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        self.barrier()
+        for k in range(steps):
+            if flush:
+                self.flusher()
+            starts[k].record(self.stream)
+            fn(k)
+            ends[k].record(self.stream)
+        self.barrier()
+        return _stats([a.elapsed_time(b) for a, b in zip(starts, ends)])
+
+    def back_to_back(self, fn, steps):
+        """One event pair around `steps` consecutive steps (nothing between the
+        launches, as in steady-state decoding); mean = elapsed / steps."""
+        s_ev = torch.cuda.Event(enable_timing=True)
+        e_ev = torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        s_ev.record(self.stream)
+        for k in range(steps):
+            fn(k)
+        e_ev.record(self.stream)
+        self.barrier()
+        mean = s_ev.elapsed_time(e_ev) / steps
+        return {"mean": mean, "median": mean, "min": mean, "max": mean}
+
+
+def capture_graph(w, ws):
+    """A CUDA graph of one decode call on ``w``'s tensors (the call's kernel
+    node(s)); ``ws`` is sized by an eager call first."""
+    import paged_attention as pa
+
+    def call():
+        return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                  w.block_size, workspace=ws)
+    call()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = call()
+    return g, out
+
+
 # ----------------------------------------------------------------------------- b200 arm
 def run_b200(args, rank, world, local_rank):
     import paged_attention as pa
-    from paged_attention import workloads
-    import oracle
 
     dist = None
     if world > 1:
@@ -241,72 +354,37 @@ def run_b200(args, rank, world, local_rank):
     flusher = L2Flush(dev)
     ws = pa.DecodeWorkspace(dev)
     stream = torch.cuda.current_stream(dev)
+    tm = Timer(stream, dev, dist, flusher)
+    peak, peak_kind = _peaks()
 
-    def op():
+    def op(_k=0):
         return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
                                   w.block_size, workspace=ws)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
 
     # ---- correctness spot-check before timing (sampled rows vs the oracle)
     out = op()
     torch.cuda.synchronize(dev)
     sample_rows = sorted({0, w.batch // 2, w.batch - 1})
-    ro, _ = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
-                                    w.block_size, batch_indices=sample_rows)
-    idx = torch.tensor(sample_rows)
-    err = (out.float().cpu()[idx] - ro[idx]).abs()
-    parity_ok = bool((err <= 2e-3 + 1e-2 * ro[idx].abs()).all())
+    parity_ok = rows_match(out[sample_rows], oracle_rows(w, sample_rows))
 
     # Inputs larger than twice the L2 stream from HBM in every step: time the
     # steps back to back. Smaller ones get the L2 flushed before every step.
     back_to_back = nbytes > 2 * L2_BYTES
-
-    def timed(fn, flush, steps):
-        """Per-step events around every step."""
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        barrier()
-        for k in range(steps):
-            if flush:
-                flusher()
-            starts[k].record(stream)
-            fn()
-            ends[k].record(stream)
-        barrier()
-        return _stats([s.elapsed_time(e) for s, e in zip(starts, ends)])
-
-    def timed_back_to_back(fn, steps):
-        """One event pair around `steps` consecutive steps (nothing between the
-        launches, as in steady-state decoding); mean = elapsed / steps."""
-        s_ev = torch.cuda.Event(enable_timing=True)
-        e_ev = torch.cuda.Event(enable_timing=True)
-        barrier()
-        s_ev.record(stream)
-        for _ in range(steps):
-            fn()
-        e_ev.record(stream)
-        barrier()
-        mean = s_ev.elapsed_time(e_ev) / steps
-        return {"mean": mean, "median": mean, "min": mean, "max": mean}
 
     # ---- eager, device-timed (the headline)
     for _ in range(args.warmup):
         if not back_to_back:
             flusher()
         op()
-    barrier()
+    tm.barrier()
     with ClockSampler(dev.index) as clocks:
-        eager = timed_back_to_back(op, args.steps) if back_to_back else timed(op, True, args.steps)
+        eager = tm.back_to_back(op, args.steps) if back_to_back else tm.per_step(op, args.steps)
     # the same steps with L2 flushed before each (reported beside the headline)
-    eager_flushed = eager if not back_to_back else timed(op, True, args.steps)
+    eager_flushed = eager if not back_to_back else tm.per_step(op, args.steps)
 
     # ---- graph replay (one kernel node), same flush discipline
-    runner = pa.PagedAttnGraphRunner(w.batch, w.num_heads, 128, max(w.seq_list()), w.block_size,
-                                     w.k_cache.shape[0], device=dev, dtype=w.dtype,
+    runner = pa.PagedAttnGraphRunner(w.batch, w.num_heads, w.q.shape[-1], max(w.seq_list()),
+                                     w.block_size, w.k_cache.shape[0], device=dev, dtype=w.dtype,
                                      num_kv_heads=w.num_kv_heads,
                                      dynamic_seq_lens=not isinstance(w.seq_len, int),
                                      max_seq_len=w.block_table.shape[1] * w.block_size)
@@ -317,29 +395,12 @@ def run_b200(args, rank, world, local_rank):
     for _ in range(args.warmup):
         flusher()
         runner.replay_only()
-    barrier()
-    gs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ge = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for k in range(args.steps):
-        flusher()
-        gs[k].record(stream)
-        runner.replay_only()
-        ge[k].record(stream)
-    barrier()
-    graph = _stats([s.elapsed_time(e) for s, e in zip(gs, ge)])
+    graph = tm.per_step(lambda _k: runner.replay_only(), args.steps)
     # reference Layer-3 method (tests/benchmark_core.py:133-145): back-to-back
     # replays averaged, no flush
-    reps = 200
     for _ in range(10):
         runner.replay_only()
-    b2b_s = torch.cuda.Event(enable_timing=True)
-    b2b_e = torch.cuda.Event(enable_timing=True)
-    b2b_s.record(stream)
-    for _ in range(reps):
-        runner.replay_only()
-    b2b_e.record(stream)
-    torch.cuda.synchronize(dev)
-    graph_b2b_ms = b2b_s.elapsed_time(b2b_e) / reps
+    graph_b2b_ms = tm.back_to_back(lambda _k: runner.replay_only(), 200)["mean"]
     del runner
 
     # ---- eager with a host sync before each step (reference method: launch
@@ -358,6 +419,101 @@ def run_b200(args, rank, world, local_rank):
     eager_sync = _stats(sync_ms)
 
     # ---- end to end through the public API with pinned host buffers
+    e2e, e2e_serial, h2d, d2h, e2e_ok = end_to_end(w, ws, out, tm, args, back_to_back)
+
+    # ---- max over ranks
+    eager_mean, graph_mean, e2e_mean, sync_med, graph_b2b, flushed_mean, e2e_serial_mean = (
+        max_over_ranks([eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"],
+                        graph_b2b_ms, eager_flushed["mean"], e2e_serial["mean"]], dist, dev))
+
+    # ---- verification all-gather over NCCL (outside the timed region)
+    if dist is not None:
+        parity_ok = gather_and_verify(out, parity_ok, args.config, rank, world, dist, dev)
+    status = ws.read_status()
+    del w, out
+
+    # ---- the head-sharded C5 step at this N (every rank takes part)
+    c5 = c5_sharded(args, rank, world, dist, dev, tm, peak)
+
+    # ---- the short steps, one GPU
+    per_cfg = per_config(args, dev, tm, peak) if world == 1 else None
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return None
+
+    total_bytes = nbytes * world
+    value = total_bytes / (eager_mean * 1e-3) / 1e9
+    achieved = nbytes / (eager["mean"] * 1e-3) / 1e9
+    traffic = _profile_traffic() if args.config == "c2" else None
+    w0 = build_shard(args.config, 0, world, dev)
+    cpu = cpu_baseline(w0, args) if world == 1 else None
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(eager_mean, 5),
+        "higher_is_better": True,
+        "scaling": "strong" if args.config == "c5" else "weak",
+        "vs_baseline": None,
+        "dtype": _dtype_name(w0.dtype),
+        "data": "synthetic (seeded N(0,1) q/K/V, shuffled page pool)",
+        "config": workload_config(w0, world, nbytes),
+        "us_per_step": {"eager": round(eager_mean * 1e3, 2),
+                        "eager_l2_flushed": round(flushed_mean * 1e3, 2),
+                        "graph_l2_flushed": round(graph_mean * 1e3, 2),
+                        "eager_host_sync": round(sync_med * 1e3, 2),
+                        "graph_back_to_back": round(graph_b2b * 1e3, 2),
+                        "eager_l2_flushed_median": round(eager_flushed["median"] * 1e3, 2),
+                        "graph_median": round(graph["median"] * 1e3, 2)},
+        "graph_gbs": round(total_bytes / (graph_mean * 1e-3) / 1e9, 1),
+        "pct_of_peak": {"eager": round(100 * value / world / peak, 1),
+                        "graph": round(100 * total_bytes / world / (graph_mean * 1e-3) / 1e9
+                                       / peak, 1),
+                        "nominal_8TBs_eager": round(100 * value / world / 8000.0, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "frac_l2_flushed": round(nbytes / (eager_flushed["mean"] * 1e-3) / 1e9
+                                              / peak, 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)"
+                     if peak_kind == "measured" else "fallback",
+                     "traffic": traffic},
+        "e2e": {"value": round(total_bytes / (e2e_mean * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "us_per_step": round(e2e_mean * 1e3, 2),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "us_per_step_copies_serialised": round(e2e_serial_mean * 1e3, 2),
+                "note": ("KV cache resident in HBM; q, block table (and lengths) in from pinned "
+                         "host memory, O out, every step; "
+                         + ("copies double-buffered on two copy streams, overlapping the "
+                            "neighbouring steps' kernels" if back_to_back else
+                            "copies and kernel serialised on one stream"))},
+        "capacity": capacity(w0, eager_mean, dev),
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "parity": {"sampled_rows_vs_oracle": parity_ok, "graph_equals_eager": bool(graph_ok),
+                   "e2e_equals_device": bool(e2e_ok), "status_word": status},
+        "c5_sharded": c5,
+        "per_config": per_cfg,
+    }
+    print(json.dumps(res), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return res
+
+
+def _dtype_name(dt):
+    return str(dt).replace("torch.", "").replace("float16", "f16").replace("bfloat16", "bf16")
+
+
+def end_to_end(w, ws, out, tm, args, back_to_back):
+    """The same step through the public API with q, the block table (and the
+    lengths) copied in from pinned host memory and O copied out every step."""
+    import paged_attention as pa
     q_host = w.q.cpu().pin_memory()
     bt_host = w.block_table.cpu().pin_memory()
     sl_host = None if isinstance(w.seq_len, int) else w.seq_len.cpu().pin_memory()
@@ -368,8 +524,9 @@ def run_b200(args, rank, world, local_rank):
     h2d = q_host.numel() * q_host.element_size() + bt_host.numel() * 4 + (
         0 if sl_host is None else sl_host.numel() * 4)
     d2h = o_host.numel() * o_host.element_size()
+    stream, dev = tm.stream, tm.dev
 
-    def e2e_step():
+    def e2e_step(_k=0):
         q_dev.copy_(q_host, non_blocking=True)
         bt_dev.copy_(bt_host, non_blocking=True)
         if sl_dev is not None:
@@ -381,11 +538,11 @@ def run_b200(args, rank, world, local_rank):
 
     for _ in range(args.warmup):
         if not back_to_back:
-            flusher()
+            tm.flusher()
         e2e_step()
-    barrier()
-    e2e_serial = timed_back_to_back(e2e_step, args.steps) if back_to_back else timed(
-        e2e_step, True, args.steps)
+    tm.barrier()
+    e2e_serial = tm.back_to_back(e2e_step, args.steps) if back_to_back else tm.per_step(
+        e2e_step, args.steps)
     e2e_ok = torch.equal(o_host, out.cpu())
 
     # Serving loop: step k+1's inputs go up on one copy stream and step k-1's
@@ -406,7 +563,7 @@ def run_b200(args, rank, world, local_rank):
         out_done = [torch.cuda.Event() for _ in range(nbuf)]
         s_ev = torch.cuda.Event(enable_timing=True)
         e_ev = torch.cuda.Event(enable_timing=True)
-        barrier()
+        tm.barrier()
         s_ev.record(stream)
         s_in.wait_stream(stream)
         s_out.wait_stream(stream)
@@ -433,7 +590,7 @@ def run_b200(args, rank, world, local_rank):
                 out_done[i].record(s_out)
         stream.wait_stream(s_out)
         e_ev.record(stream)
-        barrier()
+        tm.barrier()
         mean = s_ev.elapsed_time(e_ev) / steps
         ok = all(torch.equal(h, o_host) for h in oh[:min(nbuf, steps)])
         return {"mean": mean, "median": mean, "min": mean, "max": mean}, ok
@@ -444,93 +601,135 @@ def run_b200(args, rank, world, local_rank):
         e2e_ok = e2e_ok and pipe_ok
     else:
         e2e = e2e_serial
+    return e2e, e2e_serial, h2d, d2h, e2e_ok
 
-    # ---- max over ranks
-    eager_mean, graph_mean, e2e_mean, sync_med, graph_b2b, flushed_mean, e2e_serial_mean = (
-        max_over_ranks([eager["mean"], graph["mean"], e2e["mean"], eager_sync["median"],
-                        graph_b2b_ms, eager_flushed["mean"], e2e_serial["mean"]], dist, dev))
 
-    # ---- verification all-gather over NCCL (outside the timed region)
+def c5_sharded(args, rank, world, dist, dev, tm, peak):
+    """The head-sharded C5 step at this world size (strong scaling): per-rank
+    device times (max over ranks), aggregate bandwidth, and the NCCL gather
+    check of every shard against the oracle."""
+    import paged_attention as pa
+    w = build_shard("c5", rank, world, dev)
+    nbytes = w.effective_bytes()
+    ws = pa.DecodeWorkspace(dev)
+
+    def op(_k=0):
+        return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                  w.block_size, workspace=ws)
+    out = op()
+    torch.cuda.synchronize(dev)
+    rows = [0, w.batch // 2, w.batch - 1]
+    local_ok = rows_match(out[rows], oracle_rows(w, rows))
+    steps = max(5, min(args.steps, 20))
+    for _ in range(args.warmup):
+        op()
+    eager = tm.back_to_back(op, steps)
+    flushed = tm.per_step(op, steps)
+    g, g_out = capture_graph(w, ws)
+    for _ in range(3):
+        g.replay()
+    graph_b2b = tm.back_to_back(lambda _k: g.replay(), steps)
+    graph_flushed = tm.per_step(lambda _k: g.replay(), steps)
+    torch.cuda.synchronize(dev)
+    graph_ok = bool(torch.equal(g_out, out))
+    del g
+    t_eager, t_flushed, t_graph, t_graph_flushed, nb_max = max_over_ranks(
+        [eager["mean"], flushed["median"], graph_b2b["mean"], graph_flushed["median"],
+         float(nbytes)], dist, dev)
+    ok = local_ok and graph_ok
     if dist is not None:
-        parity_ok = gather_and_verify(out, parity_ok, args.config, rank, world, dist, dev)
-
+        ok = gather_and_verify(out, ok, "c5", rank, world, dist, dev)
     status = ws.read_status()
-
-    if rank != 0:
-        if dist is not None:
-            dist.destroy_process_group()
-        return None
-
-    peak, peak_kind = _peaks()
-    total_bytes = nbytes * world
-    value = total_bytes / (eager_mean * 1e-3) / 1e9
-    achieved = nbytes / (eager["mean"] * 1e-3) / 1e9
-    traffic = _profile_traffic() if args.config == "c2" else None
-    cpu = cpu_baseline(w, args, sample_seconds=args.cpu_seconds) if world == 1 else None
-    res = {
-        "metric": METRIC,
-        "value": round(value, 1),
-        "unit": "GB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(eager_mean, 5),
-        "higher_is_better": True,
-        "scaling": "strong" if args.config == "c5" else "weak",
-        "vs_baseline": None,
-        "dtype": str(w.dtype).replace("torch.", "").replace("float16", "f16").replace(
-            "bfloat16", "bf16"),
-        "data": "synthetic (seeded N(0,1) q/K/V, shuffled page pool)",
-        "config": {
-            "workload": w.name,
-            "batch": w.batch, "num_heads": w.num_heads, "num_kv_heads": w.num_kv_heads,
-            "head_dim": 128, "block_size": w.block_size,
-            "seq_len": w.seq_len if isinstance(w.seq_len, int) else "per-row",
-            "kv_bytes_per_rank": nbytes,
-            "l2": (f"inputs {nbytes / 1e6:.0f} MB per rank > 2x L2 (126 MB): the K steps run back "
-                   "to back between one event pair, each streaming its inputs from HBM "
-                   "(per-step-event timings with L2 flushed under us_per_step)"
-                   if back_to_back else
-                   "flushed before every step: 512 MB write, then 512 MB read (no dirty lines left)"),
-            "schedule": "token-balanced persistent",
-            "parallelism": (f"kv-head shards x{world}" if world > 1 else "single GPU"),
-        },
-        "us_per_step": {"eager": round(eager_mean * 1e3, 2),
-                        "eager_l2_flushed": round(flushed_mean * 1e3, 2),
-                        "graph_l2_flushed": round(graph_mean * 1e3, 2),
-                        "eager_host_sync": round(sync_med * 1e3, 2),
-                        "graph_back_to_back": round(graph_b2b * 1e3, 2),
-                        "eager_l2_flushed_median": round(eager_flushed["median"] * 1e3, 2),
-                        "graph_median": round(graph["median"] * 1e3, 2)},
-        "graph_gbs": round(total_bytes / (graph_mean * 1e-3) / 1e9, 1),
-        "pct_of_peak": {"eager": round(100 * value / world / peak, 1),
-                        "graph": round(100 * total_bytes / world / (graph_mean * 1e-3) / 1e9
-                                       / peak, 1),
-                        "nominal_8TBs_eager": round(100 * value / world / 8000.0, 1)},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy)"
-                     if peak_kind == "measured" else "fallback",
-                     "traffic": traffic},
-        "e2e": {"value": round(total_bytes / (e2e_mean * 1e-3) / 1e9, 1), "unit": "GB/s",
-                "us_per_step": round(e2e_mean * 1e3, 2),
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "us_per_step_copies_serialised": round(e2e_serial_mean * 1e3, 2),
-                "note": ("KV cache resident in HBM; q, block table (and lengths) in from pinned "
-                         "host memory, O out, every step; "
-                         + ("copies double-buffered on two copy streams, overlapping the "
-                            "neighbouring steps' kernels" if back_to_back else
-                            "copies and kernel serialised on one stream"))},
-        "capacity": capacity(w, eager_mean, dev),
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-        "cpu_baseline": cpu,
-        "parity": {"sampled_rows_vs_oracle": parity_ok, "graph_equals_eager": bool(graph_ok),
-                   "e2e_equals_device": bool(e2e_ok), "status_word": status},
+    total = nbytes * world
+    name = w.name.split("_rank")[0]
+    del w, out, g_out
+    torch.cuda.empty_cache()
+    return {
+        "workload": f"{name} (8 KV heads in {world} shard(s))",
+        "scaling": "strong", "ranks": world, "kv_heads_per_rank": 8 // world,
+        "q_heads_per_rank": 64 // world, "bytes_total": total, "bytes_per_rank": int(nb_max),
+        "l2": "inputs per rank > 2x L2: back to back between one event pair; L2-flushed "
+              "per-step medians beside",
+        "us_per_step": {"eager": round(t_eager * 1e3, 1),
+                        "eager_l2_flushed_median": round(t_flushed * 1e3, 1),
+                        "graph_back_to_back": round(t_graph * 1e3, 1),
+                        "graph_l2_flushed_median": round(t_graph_flushed * 1e3, 1)},
+        "gbs_aggregate": round(total / (t_eager * 1e-3) / 1e9, 1),
+        "gbs_per_rank": round(nb_max / (t_eager * 1e-3) / 1e9, 1),
+        "frac_per_rank": round(nb_max / (t_eager * 1e-3) / 1e9 / peak, 4),
+        "frac_per_rank_l2_flushed": round(nb_max / (t_flushed * 1e-3) / 1e9 / peak, 4),
+        "verified": bool(ok), "status_word": status, "steps": steps,
     }
-    print(json.dumps(res), flush=True)
-    if dist is not None:
-        dist.destroy_process_group()
+
+
+PER_CONFIG = ("c1", "c3", "c4")
+
+
+def per_config(args, dev, tm, peak):
+    """C1, C3 and C4 on one GPU: L2-flushed per step (eager, graph), back to
+    back over rotating input copies (cold in L2 without a flush), and
+    back-to-back graph replays of one input (the reference's Layer-3 method,
+    tests/benchmark_core.py:133-145; the latency target of C1)."""
+    import paged_attention as pa
+    from paged_attention import workloads
+    res = {}
+    steps = max(args.steps, 50)
+    for name in PER_CONFIG:
+        base = workloads.CONFIGS[name](dev)
+        nbytes = base.effective_bytes()
+        copies = max(2, min(128, -(-2 * L2_BYTES // nbytes)))
+        ws_list = [base] + [workloads.CONFIGS[name](dev, seed=SEEDS[name] + 100 * i)
+                            for i in range(1, copies)]
+        spaces = [pa.DecodeWorkspace(dev) for _ in ws_list]
+
+        def op_i(i):
+            w = ws_list[i % copies]
+            return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                      w.block_size, workspace=spaces[i % copies])
+        outs = [op_i(i) for i in range(copies)]
+        torch.cuda.synchronize(dev)
+        rows = sorted({0, base.batch - 1})
+        ok = rows_match(outs[0][rows], oracle_rows(base, rows))
+        for _ in range(args.warmup):
+            tm.flusher()
+            op_i(0)
+        flushed = tm.per_step(lambda _k: op_i(0), steps)
+        for i in range(copies * 2):
+            op_i(i)
+        rotating = tm.back_to_back(op_i, steps)
+        graphs = [capture_graph(w, sp) for w, sp in zip(ws_list, spaces)]
+        for i in range(copies):
+            graphs[i][0].replay()
+        torch.cuda.synchronize(dev)
+        graph_ok = all(torch.equal(g_out, o) for (_, g_out), o in zip(graphs, outs))
+        g_flushed = tm.per_step(lambda _k: graphs[0][0].replay(), steps)
+        g_rotating = tm.back_to_back(lambda k: graphs[k % copies][0].replay(), steps)
+        for _ in range(10):
+            graphs[0][0].replay()
+        g_warm = tm.back_to_back(lambda _k: graphs[0][0].replay(), 200)
+        status = max(sp.read_status() for sp in spaces)
+        plan = pa.decode_plan(base.q, base.k_cache, base.v_cache, base.block_table,
+                              base.seq_len, base.block_size)
+
+        def entry(ms):
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            return {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+        r = {"workload": base.name, "bytes": nbytes, "dtype": _dtype_name(base.dtype),
+             "eager_l2_flushed_median": entry(flushed["median"]),
+             "graph_l2_flushed_median": entry(g_flushed["median"]),
+             "eager_back_to_back_rotating": entry(rotating["mean"]),
+             "graph_back_to_back_rotating": entry(g_rotating["mean"]),
+             "graph_back_to_back_same_input": entry(g_warm["mean"]),
+             "rotating_copies": copies,
+             "kernels_per_call": plan["kernels"],
+             "parity": {"sampled_rows_vs_oracle": ok, "graph_equals_eager": bool(graph_ok),
+                        "status_word": status}}
+        if name == "c1":
+            r["target_graph_us"] = 10.0
+            r["meets_target"] = bool(g_warm["mean"] * 1e3 <= 10.0)
+        res[name] = r
+        del graphs, outs, ws_list, spaces, base
+        torch.cuda.empty_cache()
     return res
 
 
@@ -540,7 +739,7 @@ def capacity(w, step_ms, dev):
     of KV, and how many such requests fit in 90 % of the device's memory (the
     reference uses a fixed 8 GB budget)."""
     e = w.q.element_size()
-    kv = sum(w.seq_list()) * w.num_kv_heads * 128 * e * 2
+    kv = sum(w.seq_list()) * w.num_kv_heads * w.q.shape[-1] * e * 2
     per_req = kv / w.batch
     total = torch.cuda.get_device_properties(dev).total_memory
     return {"kv_mb_per_request": round(per_req / 2**20, 2),
@@ -549,29 +748,54 @@ def capacity(w, step_ms, dev):
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_baseline(w, args, sample_seconds=15.0):
-    """The reference algorithm's CPU path on a bounded sample of the workload."""
-    import oracle
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    q = w.q.cpu()
-    k = w.k_cache.cpu()
-    v = w.v_cache.cpu()
-    bt = w.block_table.cpu()
-    lens = w.seq_list()
+class CpuPath:
+    """The reference algorithm's CPU path (the oracle's FP32 gather + softmax
+    attention, tests/correctness.py:17-20) over one workload held in host
+    memory, one row per call on every host thread. Both arms time it with
+    this class, so they report the same number for the same workload."""
+
+    WARMUP_ROWS = 4
+
+    def __init__(self, w):
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.q = w.q.cpu()
+        self.k = w.k_cache.cpu()
+        self.v = w.v_cache.cpu()
+        self.bt = w.block_table.cpu()
+        self.lens = w.seq_list()
+        self.batch, self.block_size = w.batch, w.block_size
+        e = self.q.element_size()
+        self.row_bytes = [s * w.num_kv_heads * w.q.shape[-1] * e * 2
+                          + w.num_heads * w.q.shape[-1] * e * 2 for s in self.lens]
+        self.next_row = 0
+        for _ in range(self.WARMUP_ROWS):
+            self.row()
+
+    def row(self):
+        """One row (round robin over the batch); returns its algorithmic bytes."""
+        import oracle
+        b = self.next_row % self.batch
+        self.next_row += 1
+        oracle.decode_reference(self.q, self.k, self.v, self.bt, self.lens, self.block_size,
+                                batch_indices=[b])
+        return self.row_bytes[b]
+
+
+def cpu_baseline(w, args):
+    """The CPU path on a bounded sample (about ``--cpu-seconds`` of work)."""
+    cpu = CpuPath(w)
     rows_done, bytes_done, t0 = 0, 0, time.perf_counter()
-    e = q.element_size()
     while True:
-        b = rows_done % w.batch
-        oracle.decode_reference(q, k, v, bt, lens, w.block_size, batch_indices=[b])
-        bytes_done += (lens[b] * w.num_kv_heads * 128 * e * 2 + w.num_heads * 128 * e * 2)
+        bytes_done += cpu.row()
         rows_done += 1
-        if time.perf_counter() - t0 > sample_seconds:
+        if time.perf_counter() - t0 > args.cpu_seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(bytes_done / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+    return {"value": round(bytes_done / dt / 1e9, 3), "unit": "GB/s", "cores": cpu.threads,
             "kind": "port",
-            "sample": f"{rows_done} of {w.batch} rows ({dt:.1f} s), same seeded workload",
+            "sample": f"{rows_done} rows of {w.batch} round robin ({dt:.1f} s), same seeded "
+                      f"workload, torch CPU FP32, {cpu.threads} threads",
             "us_per_row": round(dt / rows_done * 1e6, 1)}
 
 
@@ -579,41 +803,32 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     from paged_attention import workloads
-    import oracle
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    w = workloads.CONFIGS[args.config]("cpu")
-    q, k, v, bt = w.q, w.k_cache, w.v_cache, w.block_table
-    lens = w.seq_list()
-    e = q.element_size()
-    rows_per_step = max(1, min(w.batch, args.ref_rows))
-
-    def step(i):
-        rows = [(i * rows_per_step + j) % w.batch for j in range(rows_per_step)]
-        oracle.decode_reference(q, k, v, bt, lens, w.block_size, batch_indices=rows)
-        return sum(lens[r] * w.num_kv_heads * 128 * e * 2 + w.num_heads * 128 * e * 2
-                   for r in rows)
-
-    for i in range(args.warmup):
-        step(i)
+    w = build_shard(args.config, 0, world, "cpu")
+    nbytes = w.effective_bytes()
+    cpu = CpuPath(w)
+    rows_per_step = max(1, args.ref_rows)
+    for _ in range(args.warmup):
+        for _ in range(rows_per_step):
+            cpu.row()
     t0 = time.perf_counter()
     nb = 0
-    for i in range(args.steps):
-        nb += step(i)
+    for _ in range(args.steps):
+        for _ in range(rows_per_step):
+            nb += cpu.row()
     dt = time.perf_counter() - t0
     gbs = nb / dt / 1e9
-    sample = (f"{rows_per_step} of {w.batch} rows per step (bounded sample of {w.name}), "
-              f"torch CPU FP32, {threads} threads")
+    sample = (f"{rows_per_step} rows per step round robin over the {w.batch} rows (bounded "
+              f"sample of {w.name}), torch CPU FP32, {cpu.threads} threads")
     res = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if args.config == "c5" else "weak", "vs_baseline": None,
+        "dtype": "f32",
         "data": "synthetic (seeded N(0,1) q/K/V, shuffled page pool)",
-        "config": {"workload": w.name, "batch": w.batch, "num_heads": w.num_heads,
-                   "num_kv_heads": w.num_kv_heads, "head_dim": 128, "block_size": w.block_size},
+        "config": workload_config(w, world, nbytes),
         "impl": "reference",
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -630,7 +845,7 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--ref-rows", type=int, default=2)
+    ap.add_argument("--ref-rows", type=int, default=8)
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -53,7 +53,7 @@ typedef enum pa_dtype { PA_F16 = 0, PA_BF16 = 1 } pa_dtype_t;
 /* Bits of the optional device status word (OR-ed by the kernel). */
 #define PA_STATUS_BAD_BLOCK 1u    /* a block-table entry outside [0, num_blocks) */
 #define PA_STATUS_BAD_SEQLEN 2u   /* seq_lens[b] < 0 or > max_blocks * block_size (clamped) */
-#define PA_STATUS_TIMEOUT 4u      /* a bounded wait on a copy barrier gave up */
+#define PA_STATUS_TIMEOUT 4u      /* a bounded wait on a copy barrier gave up (2 s) */
 
 /* One decode step: O[b, h] = softmax(q[b, h] . K_b^T * scale) V_b, where token t
  * of sequence b lives at cache[block_table[b, t / block_size], t % block_size,
@@ -108,7 +108,31 @@ typedef struct pa_decode_params {
 PA_API pa_status_t pa_decode_workspace(const pa_decode_params* p, size_t* workspace_bytes,
                                 size_t* counter_count);
 
-/* Launch one decode step on `stream` (one kernel). */
+/* The schedule pa_decode would run for these parameters (pointers are not
+ * read). Replaces nothing in the reference, whose schedule is fixed by the
+ * num_splits heuristic (paged_attention/torch_kernel.py:19-25) and its two
+ * launch grids (torch_kernel.py:37-62); it lets a caller or a test see which
+ * kernels one call launches. */
+typedef struct pa_decode_plan_info {
+  int32_t kernel_variant;     /* 1..9: tile tokens x warps per CTA x ring depth */
+  int32_t tile_tokens, warps, stages;
+  int32_t grid;               /* CTAs of the decode kernel */
+  int32_t num_splits;         /* 0: token-balanced persistent schedule; >0: split schedule */
+  int32_t group_warps;        /* balanced: warps per merge group (1, or every warp of a CTA) */
+  int32_t merge_rows_global;  /* balanced: the warps' merge rows live in the workspace */
+  int32_t merge_pass;         /* 1: merge_segments_kernel follows the decode kernel */
+  int32_t kernels;            /* launches of one call: 0 (batch 0), 1 or 2 */
+  int32_t smem_bytes;         /* dynamic shared memory per CTA */
+  int32_t reserved;
+  size_t workspace_bytes, counter_count;   /* as pa_decode_workspace reports */
+} pa_decode_plan_info;
+
+PA_API pa_status_t pa_decode_plan(const pa_decode_params* p, pa_decode_plan_info* info);
+
+/* Launch one decode step on `stream`: the decode kernel, followed (in the same
+ * stream, as a programmatic dependent launch) by merge_segments_kernel when the
+ * plan has a merge pass. If the call returns PA_ERR_LAUNCH after the first
+ * kernel was queued, `out` and `lse` are undefined for that step. */
 PA_API pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream);
 
 /* New tokens' K/V rows into the paged caches (the step before decode in a
@@ -150,6 +174,8 @@ PA_API pa_status_t pa_cache_append(const pa_append_params* p, cudaStream_t strea
  *    the library keeps it until the process exits. A call whose scratch
  *    (partials + counters, as pa_decode_workspace reports) does not fit is
  *    rejected with PA_ERR_WORKSPACE, before anything is launched.
+ *    Rejections for bad arguments, strides or alignment (PA_ERR_ARG) and for
+ *    size happen before anything is queued on `stream`.
  *  - The first call on each device looks up the array's device address once
  *    (cudaGetSymbolAddress, with that device current); make that first call
  *    before any stream capture.
@@ -165,6 +191,16 @@ PA_API pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t str
 /* max(1, min(ceil(S / block_size), max(1, 4 * sm_count / (batch * heads)))). */
 PA_API int32_t pa_num_splits_heuristic(int32_t batch, int32_t heads, int32_t seq_len,
                                 int32_t block_size, int32_t sm_count);
+
+/* Self-test of the decode kernel's bounded barrier wait, its only device-side
+ * failure handling (the reference has none). One warp waits on a barrier that
+ * nothing completes: after `limit_ns` (1 us .. 100 ms, else PA_ERR_ARG) the
+ * wait gives up, ORs PA_STATUS_TIMEOUT into *status and, as the decode kernel
+ * does, waits (bounded) for its other copy in flight -- 256 bytes from `src`,
+ * which it writes to `dst` (16-byte aligned) -- and returns. The context stays
+ * usable. */
+PA_API pa_status_t pa_selftest_wait_timeout(const void* src, void* dst, uint64_t limit_ns,
+                                            uint32_t* status, cudaStream_t stream);
 
 /* Streaming copy of `bytes` (multiple of 16, 16-byte aligned pointers): the
  * HBM peak-bandwidth probe. */

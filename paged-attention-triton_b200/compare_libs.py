@@ -4,6 +4,7 @@
     python compare_libs.py --head-dims 64,256 [--iters 50]
     python compare_libs.py --long [--iters 50]
     python compare_libs.py --small-batch [--iters 50]
+    python compare_libs.py --reference [PATH] [--configs c1,c2,c3] [--iters 50]
 
 ``--head-dims`` runs C2-sized MHA steps (B=32, S=1024, block 16, fp16, 537 MB
 of K/V) at other head dimensions instead of the five configurations (query
@@ -29,6 +30,20 @@ block]``; the caches are re-laid out once, outside the timed region. FlashInfer
 reads the ``[blocks, block, Hkv, D]`` (NHD) layout this operator uses.
 Timing: L2 flushed before every call (512 MB write, then 512 MB read), CUDA
 events around the call only, median of ``--iters`` calls.
+
+``--reference [PATH]`` times the reference's own Triton operator instead: the
+unmodified ``paged_attention`` package of bw-won/paged-attention-triton,
+imported from ``PATH`` (default ``baseline/_ref`` at the repository root, where
+it is pip-installed) under another module name, on the shapes it supports
+(C1-C3: one KV head per query head, one length for every row). Its stock call
+``paged_attention(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size)``
+(``paged_attention/torch_kernel.py:71-73``; the ``num_splits`` heuristic of
+``torch_kernel.py:19-25`` on this GPU) and its ``PagedAttnGraphRunner``
+(``paged_attention/graph_runner.py:8-45``) are timed beside this operator's
+eager call and graph runner: L2 flushed per call (eager and graph replay), and
+back-to-back graph replays with nothing between them (the reference's Layer-3
+method, ``tests/benchmark_core.py:133-145``). The reference's outputs (eager and
+graph) are checked against this operator's within the parity tolerance.
 """
 from __future__ import annotations
 
@@ -141,6 +156,101 @@ def _flashinfer_runner(w, lens_list, scale):
     return run, None
 
 
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _import_reference(path):
+    """The reference package ``paged_attention`` found under ``path``, imported
+    as ``reference_paged_attention`` (this package owns the name
+    ``paged_attention``)."""
+    import importlib.util
+    init = os.path.join(path, "paged_attention", "__init__.py")
+    if not os.path.exists(init):
+        return None, f"reference package not found under {path}"
+    spec = importlib.util.spec_from_file_location(
+        "reference_paged_attention", init,
+        submodule_search_locations=[os.path.dirname(init)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["reference_paged_attention"] = mod
+    try:
+        spec.loader.exec_module(mod)
+    except Exception as e:  # noqa: BLE001 -- e.g. Triton missing
+        return None, f"reference import failed: {type(e).__name__}: {str(e)[:160]}"
+    return mod, None
+
+
+def _time_back_to_back(fn, reps=200):
+    """Mean of ``reps`` calls between one event pair, nothing between them."""
+    for _ in range(10):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1e3 / reps
+
+
+def run_reference(a, flush):
+    """This operator against the reference's Triton operator, same inputs; the
+    reference's outputs are checked against this operator's (whose parity with
+    the oracle the GPU tests establish)."""
+    ref, err = _import_reference(a.reference)
+    if err:
+        print(json.dumps({"reference": "unavailable", "why": err}), flush=True)
+        return
+    for name in a.configs.split(","):
+        w = workloads.CONFIGS[name]("cuda")
+        if w.num_heads != w.num_kv_heads or not isinstance(w.seq_len, int):
+            print(json.dumps({"config": w.name, "reference": "shape not supported by the "
+                              "reference (grouped KV heads or per-row lengths)"}), flush=True)
+            continue
+        nb = w.k_cache.shape[0]
+        res = {"config": w.name, "bytes": w.effective_bytes()}
+
+        # this operator
+        ws = pa.DecodeWorkspace("cuda")
+
+        def mine():
+            return pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                      w.block_size, workspace=ws)
+        mine_out = mine().clone()
+        res["this_eager_us"] = _time(mine, flush, a.iters)
+        runner = pa.PagedAttnGraphRunner(w.batch, w.num_heads, w.q.shape[-1], w.seq_len,
+                                         w.block_size, nb, device="cuda", dtype=w.dtype)
+        runner.run(w.q, w.k_cache, w.v_cache, w.block_table, copy_kv=True)
+        res["this_graph_us"] = _time(runner.replay_only, flush, a.iters)
+        res["this_graph_back_to_back_us"] = _time_back_to_back(runner.replay_only)
+        del runner
+
+        # the reference, stock call and stock graph runner
+        def theirs():
+            return ref.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                       w.block_size)
+        try:
+            res["reference_matches"] = _close(theirs(), mine_out)
+            res["reference_eager_us"] = _time(theirs, flush, a.iters)
+            rr = ref.PagedAttnGraphRunner(w.batch, w.num_heads, w.q.shape[-1], w.seq_len,
+                                          w.block_size, nb, device="cuda", dtype=w.dtype)
+            o = rr.run(w.q, w.k_cache, w.v_cache, w.block_table, copy_kv=True)
+            torch.cuda.synchronize()
+            res["reference_graph_matches"] = _close(o, mine_out)
+            res["reference_graph_us"] = _time(rr.replay_only, flush, a.iters)
+            res["reference_graph_back_to_back_us"] = _time_back_to_back(rr.replay_only)
+            del rr
+        except Exception as e:  # noqa: BLE001
+            res["reference"] = f"failed: {type(e).__name__}: {str(e)[:160]}"
+        for key in list(res):
+            if key.endswith("_us"):
+                res[key.replace("_us", "_gbs")] = round(res["bytes"] / res[key] / 1e3, 1)
+                res[key] = round(res[key], 2)
+        print(json.dumps(res), flush=True)
+        del w
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5")
@@ -148,8 +258,15 @@ def main():
     ap.add_argument("--head-dims", default="", help="e.g. 64,256: C2-sized MHA at these D")
     ap.add_argument("--long", action="store_true", help="long-context shapes")
     ap.add_argument("--small-batch", action="store_true", help="few-sequence GQA shapes")
+    ap.add_argument("--reference", nargs="?", const=os.path.join(REPO, "baseline", "_ref"),
+                    default=None, help="time the reference's Triton operator (package path)")
     a = ap.parse_args()
     flush = _Flush()
+    if a.reference is not None:
+        if a.configs == "c1,c2,c3,c4,c5":
+            a.configs = "c1,c2,c3"
+        run_reference(a, flush)
+        return
     if a.long:
         g = torch.Generator().manual_seed(7)
         ragged = torch.randint(1024, 8193, (64,), generator=g, dtype=torch.int32)

@@ -160,14 +160,15 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Waits for the barrier phase with a wall-clock bound; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) return false;
+    if (global_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -675,11 +676,12 @@ __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg
 // still in flight on the other stages, so that none lands after the exit.
 template <int NS>
 __device__ __noinline__ void drain_after_timeout(unsigned* status, uint32_t bar0, int st,
-                                                 uint32_t phase, int more) {
+                                                 uint32_t phase, int more,
+                                                 unsigned long long limit_ns = kWaitLimitNs) {
   if (status) atomicOr(status, PA_STATUS_TIMEOUT);
   for (int k = 1; k < NS && k <= more; ++k) {
     const int s2 = (st + k) % NS;
-    mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1);
+    mbar_wait(bar0 + s2 * 8, (phase >> s2) & 1, limit_ns);
   }
 }
 
@@ -1574,6 +1576,43 @@ __global__ void __launch_bounds__(512) stream_read_kernel(const uint4* __restric
 }
 
 // ----------------------------------------------------------------------------
+// Self-test of the bounded barrier wait
+// ----------------------------------------------------------------------------
+// The decode kernel's only device-side failure handling: a copy barrier that
+// never completes its phase. One warp runs the same pieces on a two-stage
+// ring: stage 0's barrier expects two arrivals and only one ever comes (no
+// copy is attached to it), so its wait gives up after `limit_ns`;
+// drain_after_timeout then flags PA_STATUS_TIMEOUT and waits (bounded) for the
+// 256-byte copy in flight on stage 1, which the warp writes to `dst` before it
+// returns. Nothing traps and nothing is left in flight.
+__global__ void __launch_bounds__(32) wait_timeout_selftest_kernel(const uint4* src, uint4* dst,
+                                                                   unsigned long long limit_ns,
+                                                                   unsigned* status) {
+  __shared__ __align__(128) uint4 buf[2][16];   // stage 0 stays empty
+  __shared__ __align__(8) uint64_t bars[2];
+  const int lane = threadIdx.x;
+  const uint32_t bar0 = smem_u32(&bars[0]);
+  if (lane == 0) {
+    mbar_init(bar0, 2);        // the second arrival never comes
+    mbar_init(bar0 + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar0) : "memory");
+    mbar_expect_tx(bar0 + 8, 256);
+    bulk_load(smem_u32(&buf[1][0]), src, 256, bar0 + 8);
+  }
+  __syncwarp();
+  if (!mbar_wait(bar0, 0, limit_ns))
+    drain_after_timeout<2>(status, bar0, 0, 0u, 1, limit_ns);
+  else   // cannot happen (one arrival of two); still, leave no copy in flight
+    mbar_wait(bar0 + 8, 0, limit_ns);
+  __syncwarp();
+  if (lane < 16) dst[lane] = buf[1][lane];
+}
+
+// ----------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------
 struct DeviceInfo {
@@ -1723,6 +1762,24 @@ static pa_status_t validate(const pa_decode_params* p) {
     if (!variant_built(p->head_dim, v, dup)) return PA_ERR_UNSUPPORTED;
   }
   if (p->block_size % 8 != 0 || p->block_size > (1 << 20)) return PA_ERR_UNSUPPORTED;
+  return PA_OK;
+}
+
+// Everything pa_decode checks before it plans: the parameters, then the
+// pointers, alignments and strides of a launch.
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+static pa_status_t validate_launch(const pa_decode_params* p) {
+  const pa_status_t v = validate(p);
+  if (v != PA_OK) return v;
+  if (!p->q || !p->k_cache || !p->v_cache || !p->block_table || !p->out) return PA_ERR_ARG;
+  if (!aligned16(p->q) || !aligned16(p->k_cache) || !aligned16(p->v_cache) || !aligned16(p->out))
+    return PA_ERR_ARG;
+  if ((p->q_stride_h % 8) || (p->q_stride_b % 8) || (p->out_stride_h % 8) || (p->out_stride_b % 8))
+    return PA_ERR_ARG;
+  if ((p->k_stride_block % 8) || (p->k_stride_slot % 8) || (p->k_stride_head % 8) ||
+      (p->v_stride_block % 8) || (p->v_stride_slot % 8) || (p->v_stride_head % 8))
+    return PA_ERR_ARG;
   return PA_OK;
 }
 
@@ -1916,7 +1973,6 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
   return true;
 }
 
-static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 #endif  // PA_HOST_PART
 
 template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum>
@@ -2060,6 +2116,87 @@ static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, dim3 grid
              : launch_merge_kernel<T, 128, false>(m, grid, stream);
 }
 
+// Kernel parameters of one call (the plan's schedule constants, the
+// workspace carve-up and the multiply-shift divisors).
+static void build_kparams(const pa_decode_params* p, const Plan& pl, KParams& kp) {
+  memset(&kp, 0, sizeof(kp));
+  kp.q = static_cast<const char*>(p->q);
+  kp.q_sb = p->q_stride_b * 2;
+  kp.q_sh = p->q_stride_h * 2;
+  kp.out = static_cast<char*>(p->out);
+  kp.o_sb = p->out_stride_b * 2;
+  kp.o_sh = p->out_stride_h * 2;
+  kp.lse = p->lse;
+  kp.bt = p->block_table;
+  kp.bt_sb = p->bt_stride_b;
+  kp.max_blocks = p->max_blocks;
+  kp.seq_lens = p->seq_lens;
+  kp.seq_len = p->seq_lens ? 0 : p->seq_len;
+  kp.B = p->batch;
+  kp.Hq = p->num_heads;
+  kp.Hkv = p->num_kv_heads;
+  kp.G = pl.G;
+  kp.QC = pl.QC;
+  kp.bs = p->block_size;
+  kp.NB = p->num_blocks;
+  kp.ns = pl.ns;
+  kp.scale_log2 = p->scale * kLog2e;
+  if (pl.ns == 0) {
+    float* ws = static_cast<float*>(p->workspace);
+    const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);
+    kp.o_part = ws;
+    kp.lse_part = ws + slots * pl.slot_cols * pl.D;
+    if (pl.wslot_global)
+      kp.wslots = ws + group_slot_bytes(pl, slots) / sizeof(float);
+  } else if (p->o_partial && p->lse_partial) {
+    kp.o_part = p->o_partial;
+    kp.lse_part = p->lse_partial;
+  } else {
+    float* ws = static_cast<float*>(p->workspace);
+    const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
+    kp.o_part = ws;
+    kp.lse_part = ws + rows * pl.D;
+  }
+  kp.counters = p->counters;
+  kp.status = p->status;
+  const int tile = kVariants[pl.variant - 1].tile;
+  kp.R = gcd_int(p->block_size, tile);
+  kp.lspt = 0;
+  while ((kp.R << kp.lspt) < tile) ++kp.lspt;
+  kp.lR = 0;
+  while ((1 << kp.lR) < kp.R) ++kp.lR;
+  kp.bs_log2 = -1;
+  for (int k = 0; k < 31; ++k)
+    if ((1 << k) == p->block_size) kp.bs_log2 = k;
+  kp.W = pl.W;
+  kp.slot_cols = pl.slot_cols;
+  kp.gsz = pl.gsz;
+  kp.zero_rows = (p->seq_lens != nullptr || p->seq_len == 0) ? 1 : 0;
+  if (pl.ns == 0) {
+    const int ngroups = pl.W / pl.gsz;
+    kp.nt_u = p->seq_lens ? 0 : (p->seq_len + tile - 1) / tile;
+    kp.per_row = p->num_kv_heads * pl.QC * kp.nt_u;
+    kp.U = p->batch * kp.per_row;            // fits int32: checked by make_plan
+    kp.P = std::max((kp.U + ngroups - 1) / ngroups, pl.gsz);
+    // Whole segments per group when that costs at most 3 % of balance: no
+    // segment then crosses a group, so no piece needs the global merge (its
+    // fence, atomic and extra round trip land on one warp of the group and
+    // make that warp the group's last).
+    const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
+    if (kp.nt_u > 0 && nseg_total >= ngroups) {
+      const long long aligned = (nseg_total + ngroups - 1) / ngroups * kp.nt_u;
+      if (aligned * 100 <= static_cast<long long>(kp.P) * 103 && aligned >= pl.gsz)
+        kp.P = static_cast<int>(aligned);
+    }
+    kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
+    kp.div_row = make_fastdiv(static_cast<uint32_t>(kp.per_row));
+    kp.div_nt = make_fastdiv(static_cast<uint32_t>(kp.nt_u));
+    kp.div_ng = make_fastdiv(static_cast<uint32_t>(ngroups));
+  }
+  kp.div_qc = make_fastdiv(static_cast<uint32_t>(pl.QC));
+  kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
+}
+
 // Whether the segments that cross group boundaries merge in
 // merge_segments_kernel rather than by the last group's warp inside the
 // decode kernel, and that kernel's grid. The pass costs a dependent launch
@@ -2141,17 +2278,41 @@ pa_status_t pa_decode_workspace(const pa_decode_params* p, size_t* workspace_byt
   return PA_OK;
 }
 
-pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
+pa_status_t pa_decode_plan(const pa_decode_params* p, pa_decode_plan_info* info) {
+  if (!info) return PA_ERR_ARG;
   const pa_status_t v = validate(p);
   if (v != PA_OK) return v;
-  if (!p->q || !p->k_cache || !p->v_cache || !p->block_table || !p->out) return PA_ERR_ARG;
-  if (!aligned16(p->q) || !aligned16(p->k_cache) || !aligned16(p->v_cache) || !aligned16(p->out))
-    return PA_ERR_ARG;
-  if ((p->q_stride_h % 8) || (p->q_stride_b % 8) || (p->out_stride_h % 8) || (p->out_stride_b % 8))
-    return PA_ERR_ARG;
-  if ((p->k_stride_block % 8) || (p->k_stride_slot % 8) || (p->k_stride_head % 8) ||
-      (p->v_stride_block % 8) || (p->v_stride_slot % 8) || (p->v_stride_head % 8))
-    return PA_ERR_ARG;
+  const int sms = sm_count(current_device());
+  if (sms <= 0) return PA_ERR_LAUNCH;
+  Plan pl;
+  const pa_status_t s = make_plan(p, sms, pl);
+  if (s != PA_OK) return s;
+  KParams kp;
+  build_kparams(p, pl, kp);
+  dim3 merge_grid(1);
+  int by_segment = 0, col_split = 0;
+  const bool post = p->batch > 0 && want_post_merge(p, pl, kp, merge_grid, by_segment, col_split);
+  const Variant& var = kVariants[pl.variant - 1];
+  memset(info, 0, sizeof(*info));
+  info->kernel_variant = pl.variant;
+  info->tile_tokens = var.tile;
+  info->warps = var.nw;
+  info->stages = var.ns;
+  info->grid = pl.grid;
+  info->num_splits = pl.ns;
+  info->group_warps = pl.ns == 0 ? pl.gsz : 0;
+  info->merge_rows_global = pl.wslot_global ? 1 : 0;
+  info->merge_pass = post ? 1 : 0;
+  info->kernels = p->batch == 0 ? 0 : (post ? 2 : 1);
+  info->smem_bytes = pl.smem;
+  info->workspace_bytes = pl.ws_bytes;
+  info->counter_count = pl.counters;
+  return PA_OK;
+}
+
+pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
+  const pa_status_t v = validate_launch(p);
+  if (v != PA_OK) return v;
   const int dev = current_device();
   const int sms = sm_count(dev);
   if (sms <= 0) return PA_ERR_LAUNCH;
@@ -2164,82 +2325,8 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   if (!aligned16(p->workspace)) return PA_ERR_ARG;
 
   KParams kp;
-  memset(&kp, 0, sizeof(kp));
-  kp.q = static_cast<const char*>(p->q);
-  kp.q_sb = p->q_stride_b * 2;
-  kp.q_sh = p->q_stride_h * 2;
-  kp.out = static_cast<char*>(p->out);
-  kp.o_sb = p->out_stride_b * 2;
-  kp.o_sh = p->out_stride_h * 2;
-  kp.lse = p->lse;
-  kp.bt = p->block_table;
-  kp.bt_sb = p->bt_stride_b;
-  kp.max_blocks = p->max_blocks;
-  kp.seq_lens = p->seq_lens;
-  kp.seq_len = p->seq_lens ? 0 : p->seq_len;
-  kp.B = p->batch;
-  kp.Hq = p->num_heads;
-  kp.Hkv = p->num_kv_heads;
-  kp.G = pl.G;
-  kp.QC = pl.QC;
-  kp.bs = p->block_size;
-  kp.NB = p->num_blocks;
-  kp.ns = pl.ns;
-  kp.scale_log2 = p->scale * kLog2e;
-  if (pl.ns == 0) {
-    float* ws = static_cast<float*>(p->workspace);
-    const size_t slots = static_cast<size_t>(2) * (pl.W / pl.gsz);
-    kp.o_part = ws;
-    kp.lse_part = ws + slots * pl.slot_cols * pl.D;
-    if (pl.wslot_global)
-      kp.wslots = ws + group_slot_bytes(pl, slots) / sizeof(float);
-  } else if (p->o_partial && p->lse_partial) {
-    kp.o_part = p->o_partial;
-    kp.lse_part = p->lse_partial;
-  } else {
-    float* ws = static_cast<float*>(p->workspace);
-    const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
-    kp.o_part = ws;
-    kp.lse_part = ws + rows * pl.D;
-  }
-  kp.counters = p->counters;
-  kp.status = p->status;
   const int tile = kVariants[pl.variant - 1].tile;
-  kp.R = gcd_int(p->block_size, tile);
-  kp.lspt = 0;
-  while ((kp.R << kp.lspt) < tile) ++kp.lspt;
-  kp.lR = 0;
-  while ((1 << kp.lR) < kp.R) ++kp.lR;
-  kp.bs_log2 = -1;
-  for (int k = 0; k < 31; ++k)
-    if ((1 << k) == p->block_size) kp.bs_log2 = k;
-  kp.W = pl.W;
-  kp.slot_cols = pl.slot_cols;
-  kp.gsz = pl.gsz;
-  kp.zero_rows = (p->seq_lens != nullptr || p->seq_len == 0) ? 1 : 0;
-  if (pl.ns == 0) {
-    const int ngroups = pl.W / pl.gsz;
-    kp.nt_u = p->seq_lens ? 0 : (p->seq_len + tile - 1) / tile;
-    kp.per_row = p->num_kv_heads * pl.QC * kp.nt_u;
-    kp.U = p->batch * kp.per_row;            // fits int32: checked by make_plan
-    kp.P = std::max((kp.U + ngroups - 1) / ngroups, pl.gsz);
-    // Whole segments per group when that costs at most 3 % of balance: no
-    // segment then crosses a group, so no piece needs the global merge (its
-    // fence, atomic and extra round trip land on one warp of the group and
-    // make that warp the group's last).
-    const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
-    if (kp.nt_u > 0 && nseg_total >= ngroups) {
-      const long long aligned = (nseg_total + ngroups - 1) / ngroups * kp.nt_u;
-      if (aligned * 100 <= static_cast<long long>(kp.P) * 103 && aligned >= pl.gsz)
-        kp.P = static_cast<int>(aligned);
-    }
-    kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
-    kp.div_row = make_fastdiv(static_cast<uint32_t>(kp.per_row));
-    kp.div_nt = make_fastdiv(static_cast<uint32_t>(kp.nt_u));
-    kp.div_ng = make_fastdiv(static_cast<uint32_t>(ngroups));
-  }
-  kp.div_qc = make_fastdiv(static_cast<uint32_t>(pl.QC));
-  kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
+  build_kparams(p, pl, kp);
 
   CUtensorMap mk, mv;
   if (!cached_cache_map(&mk, p, dev, p->k_cache, p->k_stride_block, p->k_stride_slot,
@@ -2319,7 +2406,9 @@ static void* noalloc_scratch(int dev) {
 extern "C" {
 
 pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t stream) {
-  const pa_status_t v = validate(p);
+  // every check pa_decode makes before launching, so that a rejected call
+  // queues nothing (not even the counter memset below)
+  const pa_status_t v = validate_launch(p);
   if (v != PA_OK) return v;
   const int dev = current_device();
   const int sms = sm_count(dev);
@@ -2388,6 +2477,15 @@ pa_status_t pa_cache_append(const pa_append_params* p, cudaStream_t stream) {
   const long long want = (total + 255) / 256;
   const int grid = static_cast<int>(std::min<long long>(want, 8ll * sms));
   cache_append_kernel<<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
+}
+
+pa_status_t pa_selftest_wait_timeout(const void* src, void* dst, uint64_t limit_ns,
+                                     uint32_t* status, cudaStream_t stream) {
+  if (!src || !dst || !status || !aligned16(src) || !aligned16(dst)) return PA_ERR_ARG;
+  if (limit_ns < 1000ull || limit_ns > 100000000ull) return PA_ERR_ARG;
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(static_cast<const uint4*>(src),
+                                                     static_cast<uint4*>(dst), limit_ns, status);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

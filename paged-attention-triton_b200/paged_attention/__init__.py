@@ -10,6 +10,8 @@ from .torch_kernel import (  # noqa: F401
     DecodeWorkspace,
     num_splits_heuristic,
     device_sm_count,
+    decode_params,
+    decode_plan,
 )
 from .graph_runner import PagedAttnGraphRunner  # noqa: F401
 from .cache_ops import write_kv_cache, slots_for_positions  # noqa: F401

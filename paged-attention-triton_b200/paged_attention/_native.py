@@ -102,15 +102,40 @@ class AppendParams(ctypes.Structure):
     ]
 
 
+class PlanInfo(ctypes.Structure):
+    """Mirror of ``pa_decode_plan_info``."""
+
+    _fields_ = [
+        ("kernel_variant", ctypes.c_int32),
+        ("tile_tokens", ctypes.c_int32),
+        ("warps", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("num_splits", ctypes.c_int32),
+        ("group_warps", ctypes.c_int32),
+        ("merge_rows_global", ctypes.c_int32),
+        ("merge_pass", ctypes.c_int32),
+        ("kernels", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("counter_count", ctypes.c_size_t),
+    ]
+
+
 # name -> (restype, argtypes); every function declared in include/pa_decode.h.
 _SIGNATURES = {
     "pa_decode_workspace": (ctypes.c_int, [ctypes.POINTER(DecodeParams),
                                            ctypes.POINTER(ctypes.c_size_t),
                                            ctypes.POINTER(ctypes.c_size_t)]),
+    "pa_decode_plan": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.POINTER(PlanInfo)]),
     "pa_decode": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
     "pa_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeParams), ctypes.c_void_p]),
     "pa_cache_append": (ctypes.c_int, [ctypes.POINTER(AppendParams), ctypes.c_void_p]),
     "pa_num_splits_heuristic": (ctypes.c_int32, [ctypes.c_int32] * 5),
+    "pa_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_uint64, ctypes.c_void_p,
+                                                ctypes.c_void_p]),
     "pa_stream_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.c_void_p]),
     "pa_stream_read": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,

@@ -160,6 +160,55 @@ def _decode(Q: torch.Tensor, K_Cache: torch.Tensor, V_Cache: torch.Tensor,
     return res[0] if len(res) == 1 else tuple(res)
 
 
+def decode_params(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_splits=None, *,
+                  scale=None, out=None, lse=None, kernel_variant=0) -> DecodeParams:
+    """``pa_decode_params`` for these tensors (the C ABI's argument struct), for
+    callers that go through ``ctypes`` (``_native.lib()``) instead of the
+    extension: device pointers, element strides, shapes and the lengths."""
+    p = DecodeParams()
+    p.q = Q.data_ptr()
+    p.q_stride_b, p.q_stride_h = Q.stride(0), Q.stride(1)
+    p.k_cache = K_Cache.data_ptr()
+    p.k_stride_block, p.k_stride_slot, p.k_stride_head = K_Cache.stride()[:3]
+    p.v_cache = V_Cache.data_ptr()
+    p.v_stride_block, p.v_stride_slot, p.v_stride_head = V_Cache.stride()[:3]
+    p.block_table = Block_Table.data_ptr()
+    p.bt_stride_b = Block_Table.stride(0)
+    p.max_blocks = Block_Table.shape[1]
+    if isinstance(seq_len, torch.Tensor):
+        p.seq_lens, p.seq_len = seq_len.data_ptr(), 0
+    else:
+        p.seq_lens, p.seq_len = None, int(seq_len)
+    p.batch, p.num_heads, p.head_dim = Q.shape
+    p.num_kv_heads = K_Cache.shape[2]
+    p.block_size, p.num_blocks = int(block_size), K_Cache.shape[0]
+    p.num_splits = 0 if num_splits is None else int(num_splits)
+    p.scale = (1.0 / math.sqrt(Q.shape[2])) if scale is None else float(scale)
+    p.dtype = _DTYPES[Q.dtype]
+    if out is not None:
+        p.out = out.data_ptr()
+        p.out_stride_b, p.out_stride_h = out.stride(0), out.stride(1)
+    if lse is not None:
+        p.lse = lse.data_ptr()
+    p.kernel_variant = int(kernel_variant)
+    return p
+
+
+def decode_plan(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_splits=None, *,
+                kernel_variant=0) -> dict:
+    """The schedule one ``paged_attention`` call runs on Q's device
+    (``pa_decode_plan``): kernel variant, grid, merge groups, whether the merge
+    pass follows the decode kernel, and the workspace it needs."""
+    p = decode_params(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_splits,
+                      kernel_variant=kernel_variant)
+    info = _native.PlanInfo()
+    with torch.cuda.device(Q.device):
+        rc = _native.lib().pa_decode_plan(ctypes.byref(p), ctypes.byref(info))
+    if rc != _native.PA_OK:
+        raise PagedAttentionError("pa_decode_plan", rc)
+    return {name: getattr(info, name) for name, _ in info._fields_ if name != "reserved"}
+
+
 class PagedAttentionV2Function(torch.autograd.Function):
     """Reference-named autograd wrapper (``torch_kernel.py:13-68``); inference only."""
 

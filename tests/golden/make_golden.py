@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the reference implementation.
 
 Run from the repository root, in a container that has the reference checked out
-(read-only) at /root/reference:
+(read-only), giving the path of that checkout:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 It imports the reference package ``paged_attention`` and runs its own Triton
 kernels on CPU through the Triton interpreter (``TRITON_INTERPRET=1``), with an
@@ -104,7 +104,9 @@ def make_case(ref_pkg, name, seed, dtype_name, b, h, s, bs, pool, ns, table, d=1
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
+    ref = sys.argv[1]
     sys.path.insert(0, ref)
     for case in CASES:
         make_case(ref, *case)

@@ -24,7 +24,12 @@ def test_header_declares_expected_entry_points():
     names = set(_declared_functions())
     assert {"pa_decode", "pa_decode_workspace", "pa_num_splits_heuristic", "pa_stream_copy",
             "pa_stream_read", "pa_device_sm_count", "pa_status_string",
-            "pa_abi_version", "pa_cache_append"} <= names
+            "pa_abi_version", "pa_cache_append", "pa_decode_plan",
+            "pa_selftest_wait_timeout", "pa_decode_noalloc"} <= names
+
+
+def test_ctypes_binding_covers_every_declared_function():
+    assert set(_declared_functions()) == set(_native._SIGNATURES)
 
 
 def test_library_exports_every_declared_symbol():
@@ -43,7 +48,8 @@ def test_library_has_no_cudart_runtime_dependency():
 
 
 @pytest.mark.parametrize("cname,pyname", [("pa_decode_params", "DecodeParams"),
-                                          ("pa_append_params", "AppendParams")])
+                                          ("pa_append_params", "AppendParams"),
+                                          ("pa_decode_plan_info", "PlanInfo")])
 def test_struct_layout_matches_header(tmp_path, cname, pyname):
     gcc = shutil.which("gcc")
     if not gcc:
@@ -129,3 +135,22 @@ def test_null_params_rejected():
 def test_status_strings():
     assert _native.status_string(0) == "ok"
     assert "unsupported" in _native.status_string(2)
+
+
+@pytest.mark.parametrize("limit_ns", [0, 999, 100000001, 2 ** 63])
+def test_wait_timeout_selftest_rejects_limits_out_of_range(limit_ns):
+    """Validated on the host before any CUDA call (so this runs without a GPU)."""
+    lib = _native.lib()
+    buf = ctypes.create_string_buffer(512)
+    addr = (ctypes.addressof(buf) + 15) & ~15
+    assert lib.pa_selftest_wait_timeout(addr, addr + 256, limit_ns, addr, None) == _native.PA_ERR_ARG
+
+
+def test_wait_timeout_selftest_rejects_null_and_misaligned_pointers():
+    lib = _native.lib()
+    buf = ctypes.create_string_buffer(512)
+    addr = (ctypes.addressof(buf) + 15) & ~15
+    assert lib.pa_selftest_wait_timeout(None, addr, 10 ** 6, addr, None) == _native.PA_ERR_ARG
+    assert lib.pa_selftest_wait_timeout(addr, None, 10 ** 6, addr, None) == _native.PA_ERR_ARG
+    assert lib.pa_selftest_wait_timeout(addr, addr, 10 ** 6, None, None) == _native.PA_ERR_ARG
+    assert lib.pa_selftest_wait_timeout(addr + 4, addr, 10 ** 6, addr, None) == _native.PA_ERR_ARG

@@ -112,13 +112,16 @@ def test_padded_cache_strides(pa, oracle, head_dim):
     (128, 64, 8, 1, 8192, False), (128, 64, 8, 1, 8192, True), (128, 32, 4, 1, 32768, False),
     (128, 32, 8, 4, 2048, True), (128, 24, 2, 2, 9000, False), (128, 8, 8, 1, 131072, False),
     (64, 64, 8, 1, 16384, False), (64, 16, 2, 3, 5000, True), (256, 16, 2, 1, 12000, False),
-    (256, 16, 16, 1, 16384, True)])
+    (256, 16, 16, 1, 16384, True), (128, 32, 8, 4, 2048, "zero_ends"),
+    (128, 64, 8, 3, 6000, "zero_ends")])
 def test_few_long_segments_merge_pass(pa, oracle, head_dim, hq, hkv, b, s, per_row):
     """Few segments, each spread over many CTAs: the pieces merge in the
     separate merge kernel that follows the decode kernel (one CTA per crossing
     segment, its warps over the columns and pieces), for query-head groups of
     2-8 columns and partial column chunks (G = 12), single columns spanning
-    more than 8 groups, same-length and per-row lengths, D = 64, 128, 256."""
+    more than 8 groups, same-length and per-row lengths (with zero-length
+    first and last rows, which own no tile and that pass skips), D = 64, 128,
+    256. The plan query confirms that every case takes the merge pass."""
     from paged_attention import workloads
     bs = 16
     nblk = (s + bs - 1) // bs
@@ -126,8 +129,13 @@ def test_few_long_segments_merge_pass(pa, oracle, head_dim, hq, hkv, b, s, per_r
                         seed=hq + s, device="cuda", head_dim=head_dim)
     if per_row:
         lens = torch.tensor([s - 7 * i for i in range(b)], dtype=torch.int32, device="cuda")
+        if per_row == "zero_ends":
+            lens[0] = 0
+            lens[-1] = 0
     else:
         lens = s
+    plan = pa.decode_plan(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs)
+    assert plan["merge_pass"] == 1 and plan["kernels"] == 2, plan
     ws = pa.DecodeWorkspace("cuda")
     for rep in range(2):   # the second call reuses the workspace as left by the first
         o, lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, lens, bs,

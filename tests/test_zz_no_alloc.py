@@ -64,17 +64,35 @@ def _cases():
                                              device="cuda"), 0),
         ("gqa8_bf16_split3", workloads.build("noalloc_split", 6, 16, 2, 32, torch.bfloat16, 700,
                                              22, 6 * 22, seed=33, device="cuda"), 3),
+        # one long grouped-query sequence: single-warp groups whose pieces all
+        # meet in the merge pass, the layout with the most scratch per call
+        ("gqa8_bf16_b1_s8192_merge_pass", workloads.build(
+            "noalloc_long", 1, 64, 8, 16, torch.bfloat16, 8192, 512, 512, seed=35,
+            device="cuda"), 0),
     ]
 
 
-@pytest.mark.parametrize("case", range(3))
+@pytest.mark.parametrize("case", range(4))
 def test_noalloc_matches_pa_decode_on_two_calls(case):
+    import oracle
     import paged_attention as pa
     from paged_attention import _native
     name, w, ns = _cases()[case]
+    plan = pa.decode_plan(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len, w.block_size,
+                          ns or None)
+    if name.endswith("merge_pass"):
+        assert plan["merge_pass"] == 1 and plan["group_warps"] == 1, plan
+    assert plan["workspace_bytes"] + 4 * plan["counter_count"] <= \
+        _native.PA_NOALLOC_SCRATCH_BYTES, plan
     # the existing entry point (caller-provided workspace)
     ref_o, ref_lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
                                         w.block_size, ns or None, return_lse=True)
+    # and the oracle, on sampled rows (a plan bug shared by both entry points
+    # would pass the comparison above but not this one)
+    rows = sorted({0, w.batch // 2, w.batch - 1})
+    or_o, or_lse = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, w.seq_len,
+                                           w.block_size, batch_indices=rows)
+    idx = torch.tensor(rows)
     lib = _native.lib()
     stream = torch.cuda.current_stream().cuda_stream
     for call in range(2):
@@ -88,6 +106,8 @@ def test_noalloc_matches_pa_decode_on_two_calls(case):
         torch.cuda.synchronize()
         assert_o_close(out, ref_o.float(), f"{name} call {call} O")
         assert_lse_close(lse, ref_lse, f"{name} call {call} LSE")
+        assert_o_close(out.cpu()[idx], or_o[idx], f"{name} call {call} O vs oracle")
+        assert_lse_close(lse.cpu()[idx], or_lse[idx], f"{name} call {call} LSE vs oracle")
 
 
 def test_noalloc_rejects_scratch_beyond_its_maximum():
@@ -102,3 +122,19 @@ def test_noalloc_rejects_scratch_beyond_its_maximum():
     assert need > _native.PA_NOALLOC_SCRATCH_BYTES
     rc = _native.lib().pa_decode_noalloc(ctypes.byref(p), torch.cuda.current_stream().cuda_stream)
     assert rc == _native.PA_ERR_WORKSPACE
+
+
+def test_noalloc_rejects_bad_strides_before_queuing_anything():
+    """A stride the kernel cannot use is rejected by the same checks pa_decode
+    makes, before the call touches the scratch array or the stream."""
+    from paged_attention import _native, workloads
+    w = workloads.build("noalloc_stride", 2, 8, 8, 16, torch.float16, 64, 4, 8, seed=36,
+                        device="cuda")
+    out = torch.empty_like(w.q)
+    lse = torch.empty(w.batch, w.num_heads, dtype=torch.float32, device="cuda")
+    p = _params(w.q, w.k_cache, w.v_cache, w.block_table, 64, 16, out, lse)
+    p.k_stride_slot += 1          # not a multiple of 8 elements
+    s = torch.cuda.Stream()
+    rc = _native.lib().pa_decode_noalloc(ctypes.byref(p), s.cuda_stream)
+    assert rc == _native.PA_ERR_ARG
+    assert s.query()              # nothing was queued on the stream
