@@ -124,6 +124,11 @@ struct KParams {
   FastDiv div_ng;           // by the number of groups (P with per-row lengths)
   float* wslots;            // warps' merge rows in global memory (null: shared memory)
   int post_merge;           // 1: segments that cross groups merge in merge_segments_kernel
+  // Per-row lengths, whole-CTA groups: group boundaries move to the nearest
+  // segment boundary when segments are short (max_nt: tiles of the longest
+  // possible segment), so no segment crosses a group and every merge stays in
+  // shared memory.
+  int snap, max_nt;
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -400,6 +405,31 @@ __device__ __forceinline__ void piece_of(const Cursor& c, const Ranges& rg, int&
           ((glo == c.seg_lo && ghi == seg_hi) ? kGroupSeg : 0);
 }
 
+// One warp's arrival on a counter that elects the last of `n` arrivals (the
+// warp that merges). Every lane's writes before the call are visible to the
+// last arriver, and the last arriver's lanes see every other arriver's writes:
+// a warp barrier orders the lanes' writes before lane 0's acquire-release
+// atomic, a second one orders that acquire before the lanes' later reads. No
+// sequentially consistent fence: on B200 `__threadfence()` + a relaxed atomic
+// cost ~5 us per publish in ragged steps with many pieces. kGpu: a counter in
+// global memory at GPU scope; else one in shared memory at CTA scope.
+template <bool kGpu>
+__device__ __forceinline__ bool arrive_elect_last(int* counter, int n, int lane) {
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) {
+    if constexpr (kGpu)
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                   : "=r"(old) : "l"(counter) : "memory");
+    else
+      asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                   : "=r"(old) : "r"(smem_u32(counter)) : "memory");
+  }
+  const bool last = __shfl_sync(kFull, old, 0) == n - 1;
+  __syncwarp();
+  return last;
+}
+
 __device__ __forceinline__ void flag(const KParams& p, unsigned bits) {
   if (p.status) atomicOr(p.status, bits);
 }
@@ -582,6 +612,42 @@ __device__ __forceinline__ void merge_rows(int n, int lane, const Src& src,
   lse_out = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
 }
 
+// The same rule over rows in shared memory, as one compact loop with a running
+// max (the order of split_kv_kernel.py:105-118): the merge runs once per
+// piece on the step's tail, where straight-line code is paid for in
+// instruction fetch, and shared-memory loads are short enough not to need
+// batching.
+template <int D, class Src>
+__device__ __forceinline__ void merge_rows_smem(int n, int lane, const Src& src,
+                                                RowV<HD<D>::kLaneF>& out, float& lse_out) {
+  constexpr int N = HD<D>::kLaneF;
+  float m = kValidLse, sum = 0.f;
+  RowV<N> a;
+#pragma unroll
+  for (int i = 0; i < N; ++i) a.f[i] = 0.f;
+#pragma unroll 1
+  for (int k = 0; k < n; ++k) {
+    const float* row;
+    const float* lp;
+    src(k, row, lp);
+    const float l = *lp;
+    if (l > kValidLse) {
+      const RowV<N> v = load_row<false, N>(row, lane);
+      const float mn = fmaxf(m, l);
+      const float f = exp2f((m - mn) * kLog2e);
+      const float wgt = exp2f((l - mn) * kLog2e);
+      sum = fmaf(sum, f, wgt);
+#pragma unroll
+      for (int i = 0; i < N; ++i) a.f[i] = fmaf(a.f[i], f, wgt * v.f[i]);
+      m = mn;
+    }
+  }
+  const float inv = __fdividef(1.f, fmaxf(sum, 1e-20f));
+#pragma unroll
+  for (int i = 0; i < N; ++i) out.f[i] = a.f[i] * inv;
+  lse_out = sum > 0.f ? m + __logf(sum) : kSentinel;
+}
+
 // Final output row of (b, hq): this lane's D/32 dims in the output dtype.
 template <typename T, int D>
 __device__ __forceinline__ void store_out(const KParams& p, int b, int hq, int lane,
@@ -656,15 +722,9 @@ template <typename T, int D>
 __device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg, int b, int kvh,
                                               int qc, int gc, int seg_lo, int seg_hi, int lane) {
   if (p.post_merge) return;   // the merge kernel that follows reads the slots
-  __threadfence();
-  __syncwarp();
   const int n = (seg_hi - 1) / rg.P - seg_lo / rg.P + 1;
   const int cid = (b * p.Hkv + kvh) * p.QC + qc;
-  int last = 0;
-  if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == n - 1);
-  last = __shfl_sync(kFull, last, 0);
-  if (!last) return;
-  __threadfence();
+  if (!arrive_elect_last<true>(p.counters + cid, n, lane)) return;
   merge_groups<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
   if (lane == 0) atomicExch(p.counters + cid, 0);
 }
@@ -686,14 +746,15 @@ __device__ __noinline__ void drain_after_timeout(unsigned* status, uint32_t bar0
 }
 
 // Rows of length 0 own no tile: O = 0 and LSE = -1e30 (split_kv_kernel.py:101,120).
+// With per-row lengths a row is empty when its tile prefix sum does not grow
+// (negative lengths count as 0 and are flagged by the prefix-sum pass).
 template <int D, bool kCum>
 __device__ __noinline__ void zero_length_rows(int B, int Hq, char* out, long long o_sb,
-                                              long long o_sh, float* lse, const int* seq_lens,
+                                              long long o_sh, float* lse, const int* cum,
                                               int seq_len) {
   for (int b = blockIdx.x; b < B; b += gridDim.x) {
-    // negative lengths count as 0 (and are flagged by the prefix-sum pass)
-    const int S = kCum ? max(0, __ldg(seq_lens + b)) : seq_len;
-    if (S != 0) continue;
+    const bool empty = kCum ? (cum[b + 1] == cum[b]) : (seq_len == 0);
+    if (!empty) continue;
     for (int idx = threadIdx.x; idx < Hq * (D / 8); idx += blockDim.x) {
       const int h = idx / (D / 8), c = idx % (D / 8);
       *reinterpret_cast<uint4*>(out + b * o_sb + h * o_sh + c * 16) = make_uint4(0, 0, 0, 0);
@@ -803,9 +864,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
     __syncthreads();
   }
 
-  if (!kSplit && p.zero_rows)
-    zero_length_rows<D, kCum>(p.B, p.Hq, p.out, p.o_sb, p.o_sh, p.lse, p.seq_lens, p.seq_len);
-
   const int G = p.G;
   const int spt_mask = (1 << p.lspt) - 1;
   const int bt_tiles = 32 >> p.lspt;          // tiles per page batch (one box per lane)
@@ -819,6 +877,26 @@ __global__ void __launch_bounds__(NW * 32, 1)
                                                   p.div_ng)),
                         p.gsz);
       set_ranges(U, P, p.gsz == 1 ? P : (P + NW - 1) / NW);
+      if (p.snap && P >= 2 * p.max_nt) {
+        // Both CTAs that share a boundary compute the same snapped value; a
+        // boundary moves by at most half a segment (< P / 2), so the groups
+        // stay ordered and every segment lies inside one group.
+        const int nseg = p.Hkv * p.QC;
+        auto snap = [&](long long at) -> int {
+          if (at >= U) return U;
+          const int u = static_cast<int>(at);
+          const int b = find_row(cum, p.B, u);
+          const int base = cum[b];
+          const int nt = (cum[b + 1] - base) / nseg;
+          const int lo = base + (u - base) / nt * nt;
+          return (u - lo <= lo + nt - u) ? lo : lo + nt;
+        };
+        rg.gr0 = snap(static_cast<long long>(rg.g) * P);
+        rg.gr1 = snap(static_cast<long long>(rg.g + 1) * P);
+        rg.Pw = max(1, (rg.gr1 - rg.gr0 + NW - 1) / NW);
+        rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
+        rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
+      }
     }
     n_tiles = rg.wr1 - rg.wr0;
   } else {
@@ -858,14 +936,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
       for (int d = lane; d < D; d += 32) p.o_part[row * D + d] = 0.f;
       if (lane == 0) p.lse_part[row] = kSentinel;
     }
-    __threadfence();
-    __syncwarp();
-    int last = 0;
     const int cid = (w.b * p.Hkv + w.kvh) * p.QC + w.qc;
-    if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == p.ns - 1);
-    last = __shfl_sync(kFull, last, 0);
-    if (!last) return;
-    __threadfence();
+    if (!arrive_elect_last<true>(p.counters + cid, p.ns, lane)) return;
     merge_splits<T, D>(p, w.b, w.kvh, w.qc, gc, lane);
     if (lane == 0) atomicExch(p.counters + cid, 0);
     return;
@@ -952,6 +1024,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // The next kernel in the stream may start its own prologue on SMs this grid
   // leaves; it waits for this grid's completion before touching memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Zero-length rows, while the first copies are in flight.
+  if (!kSplit && p.zero_rows)
+    zero_length_rows<D, kCum>(p.B, p.Hq, p.out, p.o_sb, p.o_sh, p.lse, cum, p.seq_len);
 
   // ---- consumer state
   uint32_t qf[H::kSteps][2];
@@ -1224,14 +1299,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
     if (kSplit) {
       // split schedule: the last split of the segment merges all ns rows
-      __threadfence();
-      __syncwarp();
       const int cid = (b * p.Hkv + kvh) * p.QC + qc;
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(p.counters + cid, 1) == p.ns - 1);
-      last = __shfl_sync(kFull, last, 0);
-      if (!last) continue;
-      __threadfence();
+      if (!arrive_elect_last<true>(p.counters + cid, p.ns, lane)) continue;
       merge_splits<T, D>(p, b, kvh, qc, gc, lane);
       if (lane == 0) atomicExch(p.counters + cid, 0);
       continue;
@@ -1243,15 +1312,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
     // Shared-memory piece: the group's last warp on this piece merges the
     // warps' rows into the group's piece.
-    __threadfence_block();
-    __syncwarp();
     const int w_first = (glo - rg.gr0) / rg.Pw;
     const int nw = (ghi - 1 - rg.gr0) / rg.Pw - w_first + 1;
-    int last = 0;
-    if (lane == 0) last = (atomicAdd(gcnt + w_first, 1) == nw - 1);
-    last = __shfl_sync(kFull, last, 0);
-    if (!last) continue;
-    __threadfence_block();
+    if (!arrive_elect_last<false>(gcnt + w_first, nw, lane)) continue;
     if (lane == 0) gcnt[w_first] = 0;
     for (int j = 0; j < gc; ++j) {
       auto src = [&](int k, const float*& row, const float*& lp) {
@@ -1263,7 +1326,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       };
       RowV<H::kLaneF> o4;
       float lse;
-      merge_rows<false, D>(nw, lane, src, o4, lse);
+      merge_rows_smem<D>(nw, lane, src, o4, lse);
       if (fl & kGroupSeg) {
         store_out<T, D>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
       } else {
@@ -1532,21 +1595,30 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const MergeParams m
 // ----------------------------------------------------------------------------
 // Bandwidth probes (replace measure_peak_bw.py:15-21's Triton copy kernel)
 // ----------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) stream_copy_kernel(const uint4* __restrict__ src,
-                                                          uint4* __restrict__ dst, size_t n) {
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; i + 3 * stride < n; i += 4 * stride) {
-    const uint4 a = __ldcs(src + i);
-    const uint4 b = __ldcs(src + i + stride);
-    const uint4 c = __ldcs(src + i + 2 * stride);
-    const uint4 d = __ldcs(src + i + 3 * stride);
-    __stcs(dst + i, a);
-    __stcs(dst + i + stride, b);
-    __stcs(dst + i + 2 * stride, c);
-    __stcs(dst + i + 3 * stride, d);
+// Each CTA copies one contiguous chunk of 256 threads x 8 x 16 B = 32 KB: all
+// eight loads of a thread are issued before its stores, and the grid covers
+// the buffer once (no grid-stride loop), so every SM keeps many independent
+// chunks in flight. On B200 this copies at ~6.86 TB/s (read + write), above a
+// device-to-device cudaMemcpy of the same buffer (~6.55 TB/s); a persistent
+// grid-stride form with 4 loads per iteration reached ~5.9 TB/s.
+constexpr int kCopyThreads = 256;
+constexpr int kCopyUnroll = 8;
+
+__global__ void __launch_bounds__(kCopyThreads) stream_copy_kernel(const uint4* __restrict__ src,
+                                                                   uint4* __restrict__ dst,
+                                                                   size_t n) {
+  const size_t base = static_cast<size_t>(blockIdx.x) * kCopyThreads * kCopyUnroll + threadIdx.x;
+  uint4 v[kCopyUnroll];
+#pragma unroll
+  for (int u = 0; u < kCopyUnroll; ++u) {
+    const size_t k = base + static_cast<size_t>(u) * kCopyThreads;
+    if (k < n) v[u] = src[k];
   }
-  for (; i < n; i += stride) __stcs(dst + i, __ldcs(src + i));
+#pragma unroll
+  for (int u = 0; u < kCopyUnroll; ++u) {
+    const size_t k = base + static_cast<size_t>(u) * kCopyThreads;
+    if (k < n) dst[k] = v[u];
+  }
 }
 
 __global__ void __launch_bounds__(512) stream_read_kernel(const uint4* __restrict__ src, size_t n,
@@ -2195,6 +2267,8 @@ static void build_kparams(const pa_decode_params* p, const Plan& pl, KParams& kp
   }
   kp.div_qc = make_fastdiv(static_cast<uint32_t>(pl.QC));
   kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
+  const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
+  kp.max_nt = static_cast<int>(std::min<long long>((cap + tile - 1) / tile, 0x3fffffff));
 }
 
 // Whether the segments that cross group boundaries merge in
@@ -2338,6 +2412,7 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   dim3 merge_grid(1);
   int by_segment = 0, col_split = 0;
   kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment, col_split) ? 1 : 0;
+  kp.snap = (pl.ns == 0 && pl.use_cum && pl.gsz > 1 && !kp.post_merge) ? 1 : 0;
 
   cudaError_t e;
   if (p->dtype == PA_F16)
@@ -2491,10 +2566,13 @@ pa_status_t pa_selftest_wait_timeout(const void* src, void* dst, uint64_t limit_
 
 pa_status_t pa_stream_copy(const void* src, void* dst, size_t bytes, cudaStream_t stream) {
   if (!src || !dst || (bytes & 15) || !aligned16(src) || !aligned16(dst)) return PA_ERR_ARG;
-  const int sms = sm_count(current_device());
-  if (sms <= 0) return PA_ERR_LAUNCH;
-  stream_copy_kernel<<<sms * 4, 512, 0, stream>>>(static_cast<const uint4*>(src),
-                                                   static_cast<uint4*>(dst), bytes / 16);
+  const size_t n = bytes / 16;
+  const size_t per_cta = static_cast<size_t>(kCopyThreads) * kCopyUnroll;
+  const size_t grid = (n + per_cta - 1) / per_cta;
+  if (grid == 0) return PA_OK;
+  if (grid > 0x7fffffffull) return PA_ERR_ARG;
+  stream_copy_kernel<<<static_cast<unsigned>(grid), kCopyThreads, 0, stream>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n);
   return cudaGetLastError() == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 }
 

@@ -173,3 +173,31 @@ def test_long_segments_merge_rows_in_workspace(pa, oracle, head_dim, hq, hkv, va
         ro, rl = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, lengths, bs)
         assert_o_close(o, ro, "O")
         assert_lse_close(lse, rl, "LSE")
+
+
+@pytest.mark.parametrize("hq,hkv,b,smax,variant", [
+    (32, 8, 128, 256, 0), (32, 8, 128, 256, 5), (32, 8, 300, 100, 5), (16, 16, 200, 300, 0),
+    (16, 16, 64, 2000, 0), (64, 8, 96, 200, 0)])
+def test_ragged_short_segments_group_boundaries(pa, oracle, hq, hkv, b, smax, variant):
+    """Ragged batches of short rows (zero-length rows included): with
+    whole-CTA merge groups the group boundaries move to segment boundaries, so
+    every segment merges inside one CTA; with longer rows they stay put and the
+    cross-CTA merge runs. Every row against the oracle."""
+    from paged_attention import workloads
+    g = torch.Generator().manual_seed(b + smax)
+    lens = torch.randint(0, smax + 1, (b,), generator=g, dtype=torch.int32)
+    lens[0] = 0
+    lens[b // 2] = smax
+    lens[-1] = 0
+    nblk = (smax + 15) // 16
+    w = workloads.build("ragged_short", b, hq, hkv, 16, torch.bfloat16, lens.cuda(), nblk,
+                        b * nblk, seed=b, device="cuda")
+    ws = pa.DecodeWorkspace("cuda")
+    for _ in range(2):
+        o, lse = pa.paged_attention(w.q, w.k_cache, w.v_cache, w.block_table, lens.cuda(), 16,
+                                    return_lse=True, workspace=ws, kernel_variant=variant)
+        torch.cuda.synchronize()
+        assert ws.read_status() == 0
+    ro, rl = oracle.decode_reference(w.q, w.k_cache, w.v_cache, w.block_table, lens, 16)
+    assert_o_close(o, ro, "O")
+    assert_lse_close(lse, rl, "LSE")
