@@ -43,7 +43,8 @@ extern "C" {
 typedef enum pa_status {
   PA_OK = 0,
   PA_ERR_ARG = 1,          /* null pointer, inconsistent shape, bad stride/alignment */
-  PA_ERR_UNSUPPORTED = 2,  /* legal but not built: head_dim not 64/128/256, block_size % 8 != 0 */
+  PA_ERR_UNSUPPORTED = 2,  /* legal but not built: head_dim not 32/64/128/256, an explicit
+                              kernel_variant the shape has no kernel for */
   PA_ERR_LAUNCH = 3,       /* CUDA runtime/driver error while launching */
   PA_ERR_WORKSPACE = 4     /* workspace or counter buffer smaller than queried */
 } pa_status_t;
@@ -96,9 +97,10 @@ typedef struct pa_decode_params {
   int32_t* counters;           /* zero-filled once by the caller; the kernel leaves it zeroed */
   size_t counter_count;
   uint32_t* status;            /* optional device word, PA_STATUS_* bits OR-ed in */
-  /* 0: automatic. 1..9: a fixed kernel variant (tile tokens x warps x ring
-   * depth), for tuning; see the variant table in csrc/pa_decode.cu (1-5 for
-   * head_dim 128; 3, 5 and 8 for 64; 6, 7 and 9 for 256; others return
+  /* 0: automatic. 1..10: a fixed kernel variant (tile tokens x warps x ring
+   * depth), for tuning; see the variant table in csrc/pa_decode.cu (1-5 and
+   * 10 for head_dim 128; 3, 5 and 8 for 64; 6, 7 and 9 for 256; others, and
+   * any variant for head_dim 32 or pages not a multiple of 8 tokens, return
    * PA_ERR_UNSUPPORTED). */
   int32_t kernel_variant;
 } pa_decode_params;
@@ -114,7 +116,7 @@ PA_API pa_status_t pa_decode_workspace(const pa_decode_params* p, size_t* worksp
  * launch grids (torch_kernel.py:37-62); it lets a caller or a test see which
  * kernels one call launches. */
 typedef struct pa_decode_plan_info {
-  int32_t kernel_variant;     /* 1..9: tile tokens x warps per CTA x ring depth */
+  int32_t kernel_variant;     /* 1..10: tile tokens x warps per CTA x ring depth */
   int32_t tile_tokens, warps, stages;
   int32_t grid;               /* CTAs of the decode kernel */
   int32_t num_splits;         /* 0: token-balanced persistent schedule; >0: split schedule */
@@ -123,7 +125,8 @@ typedef struct pa_decode_plan_info {
   int32_t merge_pass;         /* 1: merge_segments_kernel follows the decode kernel */
   int32_t kernels;            /* launches of one call: 0 (batch 0), 1 or 2 */
   int32_t smem_bytes;         /* dynamic shared memory per CTA */
-  int32_t reserved;
+  int32_t generic_path;       /* 1: head_dim 32 or pages not a multiple of 8 tokens: the
+                                 CUDA-core split + reduce kernels (kernel_variant 0) */
   size_t workspace_bytes, counter_count;   /* as pa_decode_workspace reports */
 } pa_decode_plan_info;
 

@@ -409,10 +409,9 @@ __device__ __forceinline__ void piece_of(const Cursor& c, const Ranges& rg, int&
 // warp that merges). Every lane's writes before the call are visible to the
 // last arriver, and the last arriver's lanes see every other arriver's writes:
 // a warp barrier orders the lanes' writes before lane 0's acquire-release
-// atomic, a second one orders that acquire before the lanes' later reads. No
-// sequentially consistent fence: on B200 `__threadfence()` + a relaxed atomic
-// cost ~5 us per publish in ragged steps with many pieces. kGpu: a counter in
-// global memory at GPU scope; else one in shared memory at CTA scope.
+// atomic, a second one orders that acquire before the lanes' later reads (no
+// sequentially consistent fence is needed). kGpu: a counter in global memory
+// at GPU scope; else one in shared memory at CTA scope.
 template <bool kGpu>
 __device__ __forceinline__ bool arrive_elect_last(int* counter, int n, int lane) {
   __syncwarp();
@@ -683,6 +682,67 @@ __device__ __forceinline__ void merge_groups(const KParams& p, const Ranges& rg,
                                              int qc, int gc, int seg_lo, int seg_hi, int lane) {
   const int g_first = seg_lo / rg.P;
   const int n = (seg_hi - 1) / rg.P - g_first + 1;
+  auto slot_of = [&](int k) {
+    const int g = g_first + k;
+    return 2ll * g + (max(seg_lo, g * rg.P) == g * rg.P ? 0 : 1);
+  };
+  if (n <= 4) {
+    // Few pieces (short segments split between neighbouring groups): the
+    // pieces of up to 4 query columns are loaded in one L2 round trip instead
+    // of one per column (each one is ~1 us while the grid saturates DRAM).
+    constexpr int N = HD<D>::kLaneF;
+    const float* rows[4];   // piece k's row of column 0, and its LSE
+    const float* lses[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const long long sl = slot_of(min(k, n - 1));
+      rows[k] = gslot_row<D>(p, sl, 0) + lane * N;
+      lses[k] = gslot_lse(p, sl, 0);
+    }
+    for (int j0 = 0; j0 < gc; j0 += 4) {
+      float l[4][4];
+      RowV<N> v[4][4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (j0 + jj < gc && k < n) {
+            l[jj][k] = __ldcg(lses[k] + j0 + jj);
+            v[jj][k] = load_row<true, N>(rows[k] + (j0 + jj) * D, 0);
+          } else {
+            l[jj][k] = kSentinel;
+#pragma unroll
+            for (int i = 0; i < N; ++i) v[jj][k].f[i] = 0.f;
+          }
+        }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        if (j0 + jj >= gc) break;
+        // split_kv_kernel.py:101-122
+        float gmax = kValidLse;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (l[jj][k] > kValidLse) gmax = fmaxf(gmax, l[jj][k]);
+        float gsum = 0.f;
+        RowV<N> a;
+#pragma unroll
+        for (int i = 0; i < N; ++i) a.f[i] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float wgt = (l[jj][k] > kValidLse) ? exp2f((l[jj][k] - gmax) * kLog2e) : 0.f;
+          gsum += wgt;
+#pragma unroll
+          for (int i = 0; i < N; ++i) a.f[i] = fmaf(wgt, v[jj][k].f[i], a.f[i]);
+        }
+        const float inv = __fdividef(1.f, fmaxf(gsum, 1e-20f));
+#pragma unroll
+        for (int i = 0; i < N; ++i) a.f[i] *= inv;
+        store_out<T, D>(p, b, kvh * p.G + qc * 8 + j0 + jj, lane, a,
+                        gsum > 0.f ? gmax + __logf(gsum) : kSentinel);
+      }
+    }
+    return;
+  }
   for (int j = 0; j < gc; ++j) {
     auto src = [&](int k, const float*& row, const float*& lp) {
       const int g = g_first + k;
@@ -715,19 +775,6 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, i
   }
 }
 
-// Publishes the group's piece (already written to its global slot) and merges
-// the segment if this group arrived last; with post_merge the slot is only
-// written, for merge_segments_kernel.
-template <typename T, int D>
-__device__ __forceinline__ void publish_group(const KParams& p, const Ranges& rg, int b, int kvh,
-                                              int qc, int gc, int seg_lo, int seg_hi, int lane) {
-  if (p.post_merge) return;   // the merge kernel that follows reads the slots
-  const int n = (seg_hi - 1) / rg.P - seg_lo / rg.P + 1;
-  const int cid = (b * p.Hkv + kvh) * p.QC + qc;
-  if (!arrive_elect_last<true>(p.counters + cid, n, lane)) return;
-  merge_groups<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
-  if (lane == 0) atomicExch(p.counters + cid, 0);
-}
 
 // Cold paths, out of line so that the hot path's straight-line code does not
 // interleave with them (the short steps are bound by instruction fetch).
@@ -788,6 +835,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
                                             H::kSlotStride
                            : reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
   __shared__ int warp_tot[NW];
+  // Cross-group publishes waiting until the warp has issued all its copies:
+  // [warp][2 entries][b, kvh, qc, gc, seg_lo, seg_hi].
+  __shared__ int pend_rec[kSplit ? 1 : NW][2][6];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1061,11 +1111,58 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
   }
 
+  // A piece that crosses groups is published (an arrival through L2 and, for
+  // the last arriver, the merge) only once the warp has no copy left to
+  // issue: mid-stream, the round trip under a saturated DRAM (several us)
+  // would hold back the warp's remaining tiles; after the last issue it
+  // overlaps the copies still in flight. One call site keeps the code small.
+  int npend = 0;
+  auto flush_pending = [&]() {
+    // both arrivals go out before either result is awaited
+    const int(*rec)[6] = pend_rec[kSplit ? 0 : warp];
+    auto counter = [&](const int* r) { return p.counters + (r[0] * p.Hkv + r[1]) * p.QC + r[2]; };
+    int old0 = 0, old1 = 0;
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                   : "=r"(old0) : "l"(counter(rec[0])) : "memory");
+      if (npend > 1)
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old1) : "l"(counter(rec[1])) : "memory");
+    }
+    old0 = __shfl_sync(kFull, old0, 0);
+    old1 = __shfl_sync(kFull, old1, 0);
+    __syncwarp();
+    for (int k = 0; k < npend; ++k) {
+      const int* r = rec[k];
+      const int n = (r[5] - 1) / rg.P - r[4] / rg.P + 1;
+      if ((k == 0 ? old0 : old1) != n - 1) continue;
+      merge_groups<T, D>(p, rg, r[0], r[1], r[2], r[3], r[4], r[5], lane);
+      if (lane == 0) atomicExch(counter(r), 0);
+    }
+    npend = 0;
+  };
+  auto defer_publish = [&](int b, int kvh, int qc, int gc, int seg_lo, int seg_hi) {
+    if (npend == 2) flush_pending();
+    if (lane == 0) {
+      int* r = pend_rec[kSplit ? 0 : warp][npend];
+      r[0] = b;
+      r[1] = kvh;
+      r[2] = qc;
+      r[3] = gc;
+      r[4] = seg_lo;
+      r[5] = seg_hi;
+    }
+    __syncwarp();
+    ++npend;
+  };
+
   int st = 0;
   for (int i = 0; i < n_tiles; ++i) {
     const uint32_t sk = stage0 + st * C::kStage;
     const uint32_t sv = sk + C::kKV;
     const uint32_t sq = sk + 2 * C::kKV;
+    if (!kSplit && npend > 0 && issued == n_tiles) flush_pending();
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
       drain_after_timeout<NS>(p.status, bar0, st, phase, issued - i - 1);
@@ -1306,7 +1403,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       continue;
     }
     if (dest == 1) {
-      publish_group<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+      if (!p.post_merge) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
       continue;
     }
 
@@ -1334,8 +1431,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
         if (lane == 0) *gslot_lse(p, gslot, j) = lse;
       }
     }
-    if (!(fl & kGroupSeg)) publish_group<T, D>(p, rg, b, kvh, qc, gc, seg_lo, seg_hi, lane);
+    if (!(fl & kGroupSeg) && !p.post_merge) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
   }
+  if (!kSplit && npend > 0) flush_pending();
 }
 
 #if PA_HOST_PART
@@ -1648,6 +1746,201 @@ __global__ void __launch_bounds__(512) stream_read_kernel(const uint4* __restric
 }
 
 // ----------------------------------------------------------------------------
+// CUDA-core path for the shapes the tile kernels do not cover
+// ----------------------------------------------------------------------------
+// head_dim 32, and pages of a size that is not a multiple of 8 tokens (1, 2,
+// 4, ...; the reference accepts any power of two). The reference's own two
+// stages on CUDA cores: one warp per (row, query head, split) walks its
+// tokens 32 at a time -- lane j scores token j against the query (held in
+// shared memory), then the lanes, each owning D/32 dimensions, accumulate
+// p_j V_j (split_kv_kernel.py:12-84, FP32 partials); then one warp per (row,
+// query head) merges the splits (split_kv_kernel.py:87-122). Partials are
+// [B, Hq, ns, D] and [B, Hq, ns] fp32; an empty split stores LSE -1e30.
+struct GenParams {
+  const char* q;
+  long long q_sb, q_sh;                     // bytes
+  const char* kc;
+  const char* vc;
+  long long k_sb, k_ss, k_sh, v_sb, v_ss, v_sh;   // bytes
+  const int* bt;
+  long long bt_sb;                          // elements
+  int max_blocks;
+  const int* seq_lens;
+  int seq_len;
+  int B, Hq, G, bs, NB, ns;
+  float scale_log2;
+  float* o_part;
+  float* lse_part;
+  char* out;
+  long long o_sb, o_sh;                     // bytes
+  float* lse;
+  unsigned* status;
+};
+
+template <typename T>
+__device__ __forceinline__ float half_bits_to_float(uint16_t x);
+template <>
+__device__ __forceinline__ float half_bits_to_float<__half>(uint16_t x) {
+  return __half2float(__ushort_as_half(x));
+}
+template <>
+__device__ __forceinline__ float half_bits_to_float<__nv_bfloat16>(uint16_t x) {
+  return __bfloat162float(__ushort_as_bfloat16(x));
+}
+
+// N consecutive 16-bit values at p (2N-byte aligned) as floats.
+template <typename T, int N>
+__device__ __forceinline__ void load_halfs(const char* p, float (&f)[N]) {
+  uint16_t h[N];
+  if constexpr (N == 1) {
+    h[0] = *reinterpret_cast<const uint16_t*>(p);
+  } else if constexpr (N == 2) {
+    const uint32_t v = __ldg(reinterpret_cast<const unsigned int*>(p));
+    h[0] = v & 0xffff; h[1] = v >> 16;
+  } else if constexpr (N == 4) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    h[0] = v.x & 0xffff; h[1] = v.x >> 16; h[2] = v.y & 0xffff; h[3] = v.y >> 16;
+  } else {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[2 * i] = w[i] & 0xffff;
+      h[2 * i + 1] = w[i] >> 16;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) f[i] = half_bits_to_float<T>(h[i]);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) generic_split_kernel(const GenParams g) {
+  constexpr int N = D / 32;   // dimensions per lane in the PV product
+  __shared__ float qs[4][D];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long w = static_cast<long long>(blockIdx.x) * 4 + warp;
+  if (w >= static_cast<long long>(g.B) * g.Hq * g.ns) return;
+  const int s = static_cast<int>(w % g.ns);
+  const long long rowhq = w / g.ns;          // b * Hq + hq
+  const int hq = static_cast<int>(rowhq % g.Hq);
+  const int b = static_cast<int>(rowhq / g.Hq);
+  const int kvh = hq / g.G;
+  int S = g.seq_len;
+  if (g.seq_lens) {
+    const long long cap = static_cast<long long>(g.max_blocks) * g.bs;
+    const int raw = __ldg(g.seq_lens + b);
+    S = raw < 0 ? 0 : (raw > cap ? static_cast<int>(cap) : raw);
+    if ((raw < 0 || raw > cap) && lane == 0 && s == 0 && hq == 0 && g.status)
+      atomicOr(g.status, PA_STATUS_BAD_SEQLEN);
+  }
+  const int ss = (S + g.ns - 1) / g.ns;      // torch_kernel.py:30
+  const int t0 = s * ss;
+  const int t1 = min(t0 + ss, S);
+  float* op = g.o_part + w * D;
+  if (t0 >= t1) {                            // split_kv_kernel.py:32-33: the sentinel stays
+    for (int d = lane; d < D; d += 32) op[d] = 0.f;
+    if (lane == 0) g.lse_part[w] = kSentinel;
+    return;
+  }
+  const uint16_t* qp = reinterpret_cast<const uint16_t*>(g.q + b * g.q_sb + hq * g.q_sh);
+  for (int d = lane; d < D; d += 32) qs[warp][d] = half_bits_to_float<T>(qp[d]);
+  __syncwarp();
+  float m = -INFINITY, l = 0.f, acc[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) acc[i] = 0.f;
+  for (int c = t0; c < t1; c += 32) {
+    const int t = c + lane;
+    int page = -1, slot = 0;
+    if (t < t1) {                            // split_kv_kernel.py:52-58
+      const int lb = t / g.bs;
+      page = __ldg(g.bt + b * g.bt_sb + lb);
+      slot = t - lb * g.bs;
+      if (page < 0 || page >= g.NB) {
+        if (g.status) atomicOr(g.status, PA_STATUS_BAD_BLOCK);
+        page = -1;
+      }
+    }
+    float sc = -INFINITY;                    // masked tokens score -inf (:68-69)
+    if (page >= 0) {
+      const char* kr = g.kc + page * g.k_sb + slot * g.k_ss + kvh * g.k_sh;
+      float dot = 0.f;
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        float f[8];
+        load_halfs<T, 8>(kr + i * 16, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot = fmaf(f[e], qs[warp][i * 8 + e], dot);
+      }
+      sc = dot * g.scale_log2;
+    }
+    float cm = sc;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(kFull, cm, o));
+    const float mn = fmaxf(m, cm);
+    if (mn == -INFINITY) continue;           // every page of the step was out of range
+    const float alpha = exp2f(m - mn);
+    const float pv = (sc == -INFINITY) ? 0.f : exp2f(sc - mn);
+    float ps = pv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+    l = fmaf(l, alpha, ps);
+#pragma unroll
+    for (int i = 0; i < N; ++i) acc[i] *= alpha;
+    m = mn;
+    const int nj = min(32, t1 - c);
+    for (int j = 0; j < nj; ++j) {
+      const float pj = __shfl_sync(kFull, pv, j);
+      const int pg = __shfl_sync(kFull, page, j);
+      const int sl = __shfl_sync(kFull, slot, j);
+      if (pg < 0) continue;
+      float f[N];
+      load_halfs<T, N>(g.vc + pg * g.v_sb + sl * g.v_ss + kvh * g.v_sh + lane * N * 2, f);
+#pragma unroll
+      for (int i = 0; i < N; ++i) acc[i] = fmaf(pj, f[i], acc[i]);
+    }
+  }
+  // split_kv_kernel.py:79-84: normalised partial and its LSE (natural log)
+  const float lv = fmaxf(l, 1e-20f);
+#pragma unroll
+  for (int i = 0; i < N; ++i) op[lane * N + i] = acc[i] / lv;
+  if (lane == 0) g.lse_part[w] = (m == -INFINITY) ? kSentinel : (m + log2f(lv)) * kLn2;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) generic_reduce_kernel(const GenParams g) {
+  constexpr int N = D / 32;
+  const int lane = threadIdx.x & 31;
+  const long long w = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  if (w >= static_cast<long long>(g.B) * g.Hq) return;
+  const int hq = static_cast<int>(w % g.Hq);
+  const int b = static_cast<int>(w / g.Hq);
+  const float* lp = g.lse_part + w * g.ns;
+  const float* op = g.o_part + w * g.ns * D;
+  // split_kv_kernel.py:101-122: skip LSE <= -1e29, running max, divide by
+  // max(sum, 1e-20)
+  float gmax = kValidLse, gsum = 0.f, acc[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) acc[i] = 0.f;
+  for (int s = 0; s < g.ns; ++s) {
+    const float l = lp[s];
+    if (l <= kValidLse) continue;
+    const float mn = fmaxf(gmax, l);
+    const float f = exp2f((gmax - mn) * kLog2e);
+    const float wgt = exp2f((l - mn) * kLog2e);
+    gsum = fmaf(gsum, f, wgt);
+#pragma unroll
+    for (int i = 0; i < N; ++i) acc[i] = fmaf(acc[i], f, wgt * op[s * D + lane * N + i]);
+    gmax = mn;
+  }
+  const float inv = 1.f / fmaxf(gsum, 1e-20f);
+  uint16_t* dst = reinterpret_cast<uint16_t*>(g.out + b * g.o_sb + hq * g.o_sh) + lane * N;
+#pragma unroll
+  for (int i = 0; i < N; ++i) dst[i] = Mma<T>::from_float(acc[i] * inv);
+  if (lane == 0 && g.lse) g.lse[w] = gsum > 0.f ? gmax + logf(gsum) : kSentinel;
+}
+
+// ----------------------------------------------------------------------------
 // Self-test of the bounded barrier wait
 // ----------------------------------------------------------------------------
 // The decode kernel's only device-side failure handling: a copy barrier that
@@ -1750,6 +2043,7 @@ static const Variant kVariants[] = {
     {16, 5, 2},   // 7 (head_dim 256)
     {64, 6, 2},   // 8 (head_dim 64: 16 KB K+V tiles)
     {32, 3, 2},   // 9 (head_dim 256: 32 KB K+V tiles)
+    {32, 4, 2},   // 10 (head_dim 128: 128 KB of tiles in flight per SM)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // Opt-in shared memory per CTA is 227 KB (232448 B), static plus dynamic; the
@@ -1772,7 +2066,14 @@ struct Plan {
   int smem = 0;            // dynamic shared memory of the launch
   size_t ws_bytes = 0;
   size_t counters = 0;
+  bool generic = false;    // the CUDA-core split + reduce path (uncommon shapes)
 };
+
+// Shapes the TMA tile kernels do not cover: head_dim 32, or pages that are not
+// a multiple of 8 tokens.
+static bool generic_shape(const pa_decode_params* p) {
+  return p->head_dim == 32 || p->block_size % 8 != 0;
+}
 
 #if PA_HOST_PART
 // Shared memory a variant needs before the group merge area.
@@ -1785,7 +2086,9 @@ static int smem_base() {
 static bool variant_built(int D, int variant, bool dup) {
   switch (D) {
     case 64: return variant == 3 || variant == 5 || variant == 8;
-    case 128: return variant >= 1 && variant <= 5 && (dup || (variant != 2 && variant != 4));
+    case 128:
+      return (variant >= 1 && variant <= 5 && (dup || (variant != 2 && variant != 4))) ||
+             variant == 10;
     case 256: return variant == 6 || variant == 7 || variant == 9;
     default: return false;
   }
@@ -1807,6 +2110,7 @@ static int variant_smem_base(int variant, bool dup, int D) {
     case 3: return dup ? smem_base<true, 32, 6, 2, 128>() : smem_base<false, 32, 6, 2, 128>();
     case 4: return dup ? smem_base<true, 16, 12, 2, 128>() : 0;
     case 5: return dup ? smem_base<true, 16, 8, 2, 128>() : smem_base<false, 16, 8, 2, 128>();
+    case 10: return dup ? smem_base<true, 32, 4, 2, 128>() : smem_base<false, 32, 4, 2, 128>();
     default: return dup ? smem_base<true, 32, 4, 3, 128>() : smem_base<false, 32, 4, 3, 128>();
   }
 }
@@ -1825,7 +2129,10 @@ static pa_status_t validate(const pa_decode_params* p) {
                                     static_cast<long long>(p->max_blocks) * p->block_size)
     return PA_ERR_ARG;
   if (p->kernel_variant < 0 || p->kernel_variant > kNumVariants) return PA_ERR_ARG;
-  if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) return PA_ERR_UNSUPPORTED;
+  if (p->head_dim != 32 && p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256)
+    return PA_ERR_UNSUPPORTED;
+  if (p->block_size > (1 << 20)) return PA_ERR_UNSUPPORTED;
+  if (generic_shape(p)) return p->kernel_variant == 0 ? PA_OK : PA_ERR_UNSUPPORTED;
   if (p->kernel_variant != 0) {   // an explicit variant must be built for this head_dim
     const int g = p->num_heads / p->num_kv_heads;
     const bool dup = (g == 1 || g == 2 || g == 4);
@@ -1833,7 +2140,6 @@ static pa_status_t validate(const pa_decode_params* p) {
     if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
     if (!variant_built(p->head_dim, v, dup)) return PA_ERR_UNSUPPORTED;
   }
-  if (p->block_size % 8 != 0 || p->block_size > (1 << 20)) return PA_ERR_UNSUPPORTED;
   return PA_OK;
 }
 
@@ -1898,6 +2204,27 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
   pl.QC = (pl.G + 7) / 8;
   pl.dup = (pl.G == 1 || pl.G == 2 || pl.G == 4);
   pl.D = p->head_dim;
+  if (generic_shape(p)) {
+    // One warp per (row, query head, split), four warps per CTA; splits as
+    // given, else the reference heuristic (torch_kernel.py:19-25).
+    pl.generic = true;
+    pl.variant = 0;
+    const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
+    pl.ns = p->num_splits > 0
+                ? p->num_splits
+                : pa_num_splits_heuristic(p->batch, p->num_heads,
+                                          static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap),
+                                          p->block_size, sms);
+    const long long workers = static_cast<long long>(p->batch) * p->num_heads * pl.ns;
+    if (workers > 0x7fffffffll * 4) return PA_ERR_UNSUPPORTED;
+    pl.W = static_cast<int>(std::min<long long>(workers, 0x7fffffffll));
+    pl.grid = static_cast<int>((workers + 3) / 4);
+    pl.ws_bytes = (p->o_partial && p->lse_partial)
+                      ? 0
+                      : static_cast<size_t>(workers) * (pl.D + 1) * sizeof(float);
+    pl.counters = 0;
+    return PA_OK;
+  }
   pl.variant = pick_variant(p, pl.dup);
   if (pl.variant == 0) return PA_ERR_UNSUPPORTED;
   const Variant& v = kVariants[pl.variant - 1];
@@ -2094,7 +2421,8 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   PA_BOTH(PFX, T, true, 16, 8, 3, 128)                                               \
   PA_BOTH(PFX, T, true, 32, 6, 2, 128) PA_BOTH(PFX, T, false, 32, 6, 2, 128)         \
   PA_BOTH(PFX, T, true, 16, 12, 2, 128)                                              \
-  PA_BOTH(PFX, T, true, 16, 8, 2, 128) PA_BOTH(PFX, T, false, 16, 8, 2, 128)
+  PA_BOTH(PFX, T, true, 16, 8, 2, 128) PA_BOTH(PFX, T, false, 16, 8, 2, 128)         \
+  PA_BOTH(PFX, T, true, 32, 4, 2, 128) PA_BOTH(PFX, T, false, 32, 4, 2, 128)
 #define PA_D64(PFX, T)                                                               \
   PA_BOTH(PFX, T, true, 32, 6, 2, 64) PA_BOTH(PFX, T, false, 32, 6, 2, 64)           \
   PA_BOTH(PFX, T, true, 16, 8, 2, 64) PA_BOTH(PFX, T, false, 16, 8, 2, 64)           \
@@ -2152,6 +2480,8 @@ static cudaError_t launch(const Plan& pl, const CUtensorMap& mk, const CUtensorM
       break;
     case 5:
       return launch_one<T, kDup, 16, 8, 2, 128>(pl, mk, mv, kp, stream, dev);
+    case 10:
+      return launch_one<T, kDup, 32, 4, 2, 128>(pl, mk, mv, kp, stream, dev);
     default:
       break;
   }
@@ -2186,6 +2516,69 @@ static cudaError_t launch_merge(const MergeParams& m, int D, bool cum, dim3 grid
                : launch_merge_kernel<T, 256, false>(m, grid, stream);
   return cum ? launch_merge_kernel<T, 128, true>(m, grid, stream)
              : launch_merge_kernel<T, 128, false>(m, grid, stream);
+}
+
+// The CUDA-core path: the split kernel, then the reduce kernel, on `stream`.
+static cudaError_t launch_generic(const pa_decode_params* p, const Plan& pl,
+                                  cudaStream_t stream) {
+  GenParams g;
+  memset(&g, 0, sizeof(g));
+  g.q = static_cast<const char*>(p->q);
+  g.q_sb = p->q_stride_b * 2;
+  g.q_sh = p->q_stride_h * 2;
+  g.kc = static_cast<const char*>(p->k_cache);
+  g.vc = static_cast<const char*>(p->v_cache);
+  g.k_sb = p->k_stride_block * 2;
+  g.k_ss = p->k_stride_slot * 2;
+  g.k_sh = p->k_stride_head * 2;
+  g.v_sb = p->v_stride_block * 2;
+  g.v_ss = p->v_stride_slot * 2;
+  g.v_sh = p->v_stride_head * 2;
+  g.bt = p->block_table;
+  g.bt_sb = p->bt_stride_b;
+  g.max_blocks = p->max_blocks;
+  g.seq_lens = p->seq_lens;
+  g.seq_len = p->seq_lens ? 0 : p->seq_len;
+  g.B = p->batch;
+  g.Hq = p->num_heads;
+  g.G = pl.G;
+  g.bs = p->block_size;
+  g.NB = p->num_blocks;
+  g.ns = pl.ns;
+  g.scale_log2 = p->scale * kLog2e;
+  if (p->o_partial && p->lse_partial) {
+    g.o_part = p->o_partial;
+    g.lse_part = p->lse_partial;
+  } else {
+    const size_t rows = static_cast<size_t>(p->batch) * p->num_heads * pl.ns;
+    g.o_part = static_cast<float*>(p->workspace);
+    g.lse_part = g.o_part + rows * pl.D;
+  }
+  g.out = static_cast<char*>(p->out);
+  g.o_sb = p->out_stride_b * 2;
+  g.o_sh = p->out_stride_h * 2;
+  g.lse = p->lse;
+  g.status = p->status;
+  const long long rows_hq = static_cast<long long>(p->batch) * p->num_heads;
+  const dim3 grid_split(pl.grid), grid_reduce(static_cast<unsigned>((rows_hq + 3) / 4));
+  const bool bf = p->dtype == PA_BF16;
+#define PA_GENERIC(DIM)                                                                  \
+  if (pl.D == DIM) {                                                                     \
+    if (bf) {                                                                            \
+      generic_split_kernel<__nv_bfloat16, DIM><<<grid_split, 128, 0, stream>>>(g);       \
+      generic_reduce_kernel<__nv_bfloat16, DIM><<<grid_reduce, 128, 0, stream>>>(g);     \
+    } else {                                                                             \
+      generic_split_kernel<__half, DIM><<<grid_split, 128, 0, stream>>>(g);              \
+      generic_reduce_kernel<__half, DIM><<<grid_reduce, 128, 0, stream>>>(g);            \
+    }                                                                                    \
+    return cudaGetLastError();                                                           \
+  }
+  PA_GENERIC(32)
+  PA_GENERIC(64)
+  PA_GENERIC(128)
+  PA_GENERIC(256)
+#undef PA_GENERIC
+  return cudaErrorInvalidValue;
 }
 
 // Kernel parameters of one call (the plan's schedule constants, the
@@ -2361,13 +2754,23 @@ pa_status_t pa_decode_plan(const pa_decode_params* p, pa_decode_plan_info* info)
   Plan pl;
   const pa_status_t s = make_plan(p, sms, pl);
   if (s != PA_OK) return s;
+  memset(info, 0, sizeof(*info));
+  if (pl.generic) {
+    info->tile_tokens = 32;
+    info->warps = 4;
+    info->grid = pl.grid;
+    info->num_splits = pl.ns;
+    info->kernels = p->batch == 0 ? 0 : 2;
+    info->generic_path = 1;
+    info->workspace_bytes = pl.ws_bytes;
+    return PA_OK;
+  }
   KParams kp;
   build_kparams(p, pl, kp);
   dim3 merge_grid(1);
   int by_segment = 0, col_split = 0;
   const bool post = p->batch > 0 && want_post_merge(p, pl, kp, merge_grid, by_segment, col_split);
   const Variant& var = kVariants[pl.variant - 1];
-  memset(info, 0, sizeof(*info));
   info->kernel_variant = pl.variant;
   info->tile_tokens = var.tile;
   info->warps = var.nw;
@@ -2394,9 +2797,10 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   pa_status_t s = make_plan(p, sms, pl);
   if (s != PA_OK) return s;
   if (p->batch == 0) return PA_OK;
-  if (pl.counters > p->counter_count || !p->counters) return PA_ERR_WORKSPACE;
+  if (pl.counters > 0 && (pl.counters > p->counter_count || !p->counters)) return PA_ERR_WORKSPACE;
   if (pl.ws_bytes > p->workspace_bytes || (pl.ws_bytes && !p->workspace)) return PA_ERR_WORKSPACE;
   if (!aligned16(p->workspace)) return PA_ERR_ARG;
+  if (pl.generic) return launch_generic(p, pl, stream) == cudaSuccess ? PA_OK : PA_ERR_LAUNCH;
 
   KParams kp;
   const int tile = kVariants[pl.variant - 1].tile;
@@ -2497,7 +2901,8 @@ pa_status_t pa_decode_noalloc(const pa_decode_params* p, cudaStream_t stream) {
   unsigned char* base = static_cast<unsigned char*>(noalloc_scratch(dev));
   if (!base) return PA_ERR_LAUNCH;
   // The counters must start at zero; the previous call's partials need no clearing.
-  if (cudaMemsetAsync(base, 0, counter_bytes, stream) != cudaSuccess) return PA_ERR_LAUNCH;
+  if (counter_bytes && cudaMemsetAsync(base, 0, counter_bytes, stream) != cudaSuccess)
+    return PA_ERR_LAUNCH;
   pa_decode_params q = *p;
   q.counters = reinterpret_cast<int32_t*>(base);
   q.counter_count = pl.counters;

@@ -55,9 +55,10 @@ std::tuple<int64_t, std::vector<at::Tensor>, int64_t, int64_t> decode(
   const int64_t batch = q.size(0), heads = q.size(1), dim = q.size(2);
   const int64_t nblocks = k.size(0), bs = k.size(1), kv_heads = k.size(2);
   check(k.size(3) == dim, "head_dim of Q and the caches differ");
-  check(dim == 64 || dim == 128 || dim == 256, "head_dim must be 64, 128 or 256");
+  check(dim == 32 || dim == 64 || dim == 128 || dim == 256,
+        "head_dim must be 32, 64, 128 or 256");
   check(block_size == bs, "block_size differs from the cache's block dimension");
-  check(bs % 8 == 0, "block_size must be a multiple of 8");
+  check(bs >= 1, "block_size must be positive");
   check(heads % kv_heads == 0, "Hq must be a multiple of Hkv");
   check(bt.size(0) == batch, "Block_Table rows != batch");
   check(q.stride(2) == 1 && k.stride(3) == 1 && v.stride(3) == 1 && bt.stride(1) == 1,

@@ -117,7 +117,7 @@ class PlanInfo(ctypes.Structure):
         ("merge_pass", ctypes.c_int32),
         ("kernels", ctypes.c_int32),
         ("smem_bytes", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("generic_path", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_size_t),
         ("counter_count", ctypes.c_size_t),
     ]

@@ -41,7 +41,7 @@ from . import _native
 from ._native import DecodeParams, PagedAttentionError
 from .split_kv_kernel import LSE_SENTINEL  # noqa: F401  (re-exported constant)
 
-HEAD_DIMS = (64, 128, 256)   # head dimensions the kernel is built for
+HEAD_DIMS = (32, 64, 128, 256)   # head dimensions the kernels are built for
 
 _DTYPES = {torch.float16: _native.PA_F16, torch.bfloat16: _native.PA_BF16}
 
@@ -206,7 +206,7 @@ def decode_plan(Q, K_Cache, V_Cache, Block_Table, seq_len, block_size, num_split
         rc = _native.lib().pa_decode_plan(ctypes.byref(p), ctypes.byref(info))
     if rc != _native.PA_OK:
         raise PagedAttentionError("pa_decode_plan", rc)
-    return {name: getattr(info, name) for name, _ in info._fields_ if name != "reserved"}
+    return {name: getattr(info, name) for name, _ in info._fields_}
 
 
 class PagedAttentionV2Function(torch.autograd.Function):

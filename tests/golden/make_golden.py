@@ -49,6 +49,13 @@ CASES = [
     ("mha_bf16_d64_s9_bs8_ns4_empty_split", 12, "bfloat16", 1, 2, 9, 8, 4, 4, "shuffle", 64),
     ("mha_f16_d256_s130_bs16_ns3", 13, "float16", 1, 2, 130, 16, 12, 3, "shuffle", 256),
     ("mha_bf16_d256_b2_s40_bs32_ns2", 14, "bfloat16", 2, 1, 40, 32, 6, 2, "shuffle", 256),
+    # pages of 1, 2 and 4 tokens and head_dim 32 (any power of two is a valid
+    # tl.arange bound in the reference, split_kv_kernel.py:38,49)
+    ("mha_f16_b2_s50_bs4_ns3", 21, "float16", 2, 2, 50, 4, 32, 3, "shuffle"),
+    ("mha_bf16_s23_bs2_ns4", 22, "bfloat16", 1, 2, 23, 2, 16, 4, "shuffle"),
+    ("mha_f16_s7_bs1_ns2", 23, "float16", 1, 2, 7, 1, 10, 2, "shuffle"),
+    ("mha_f16_d32_b2_s70_bs16_ns2", 24, "float16", 2, 2, 70, 16, 12, 2, "shuffle", 32),
+    ("mha_bf16_d32_s9_bs4_ns4_empty_split", 25, "bfloat16", 1, 2, 9, 4, 4, 4, "shuffle", 32),
 ]
 
 

@@ -98,13 +98,15 @@ def _params(**kw):
     ({"seq_len": 65}, _native.PA_ERR_ARG),                          # > max_blocks * bs
     ({"num_splits": -1}, _native.PA_ERR_ARG),
     ({"head_dim": 96}, _native.PA_ERR_UNSUPPORTED),
-    ({"head_dim": 32}, _native.PA_ERR_UNSUPPORTED),
+    ({"head_dim": 16}, _native.PA_ERR_UNSUPPORTED),
+    ({"head_dim": 32, "kernel_variant": 3}, _native.PA_ERR_UNSUPPORTED),    # CUDA-core path only
     ({"head_dim": 256, "kernel_variant": 3}, _native.PA_ERR_UNSUPPORTED),   # not built for 256
     ({"head_dim": 64, "kernel_variant": 1}, _native.PA_ERR_UNSUPPORTED),    # not built for 64
     ({"head_dim": 128, "kernel_variant": 6}, _native.PA_ERR_UNSUPPORTED),   # not built for 128
-    ({"kernel_variant": 10}, _native.PA_ERR_ARG),                           # no such variant
+    ({"kernel_variant": 11}, _native.PA_ERR_ARG),                           # no such variant
     ({"kernel_variant": 8}, _native.PA_ERR_UNSUPPORTED),                    # head_dim 64 only
-    ({"block_size": 12, "seq_len": 40}, _native.PA_ERR_UNSUPPORTED),
+    ({"block_size": 12, "seq_len": 40, "kernel_variant": 5}, _native.PA_ERR_UNSUPPORTED),
+    ({"block_size": 1 << 21, "max_blocks": 1, "seq_len": 40}, _native.PA_ERR_UNSUPPORTED),
 ])
 def test_host_validation_without_gpu(kw, code):
     lib = _native.lib()

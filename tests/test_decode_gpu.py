@@ -184,7 +184,7 @@ def test_ragged_mixed_long_and_short_rows(pa, oracle, group, bs, dtype):
     _check_workload(pa, oracle, w)
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4, 5, 10])
 @pytest.mark.parametrize("group,bs,dtype", [(1, 16, torch.float16), (4, 24, torch.bfloat16),
                                             (8, 128, torch.bfloat16), (3, 8, torch.float16)])
 def test_kernel_variants(pa, oracle, variant, group, bs, dtype):
