@@ -1111,39 +1111,45 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
   }
 
-  // A piece that crosses groups is published (an arrival through L2 and, for
-  // the last arriver, the merge) only once the warp has no copy left to
-  // issue: mid-stream, the round trip under a saturated DRAM (several us)
-  // would hold back the warp's remaining tiles; after the last issue it
-  // overlaps the copies still in flight. One call site keeps the code small.
-  int npend = 0;
-  auto flush_pending = [&]() {
-    // both arrivals go out before either result is awaited
+  // A piece that crosses groups is published in two steps. Its arrival (an
+  // acquire-release atomic through L2) goes out once the warp has no copy left
+  // to issue: mid-stream, the round trip under a saturated DRAM (several us)
+  // would hold back the warp's remaining tiles, while after the last issue it
+  // overlaps the copies still in flight. The merge, for the last arriver, runs
+  // after the warp's last tile, when none of the stream's registers are live
+  // (one copy of the merge code, and no register pressure on the hot loop).
+  int npend = 0, narr = 0;     // pending publishes; how many have arrived
+  unsigned merge_mask = 0;     // pending entries this warp arrived last on
+  auto pend_counter = [&](const int* r) {
+    return p.counters + (r[0] * p.Hkv + r[1]) * p.QC + r[2];
+  };
+  auto arrive_pending = [&]() {
+    // every arrival not yet made goes out before any result is awaited
     const int(*rec)[6] = pend_rec[kSplit ? 0 : warp];
-    auto counter = [&](const int* r) { return p.counters + (r[0] * p.Hkv + r[1]) * p.QC + r[2]; };
     int old0 = 0, old1 = 0;
     __syncwarp();
     if (lane == 0) {
-      asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                   : "=r"(old0) : "l"(counter(rec[0])) : "memory");
+      if (narr == 0)
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                     : "=r"(old0) : "l"(pend_counter(rec[0])) : "memory");
       if (npend > 1)
         asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
-                     : "=r"(old1) : "l"(counter(rec[1])) : "memory");
+                     : "=r"(old1) : "l"(pend_counter(rec[1])) : "memory");
     }
     old0 = __shfl_sync(kFull, old0, 0);
     old1 = __shfl_sync(kFull, old1, 0);
     __syncwarp();
-    for (int k = 0; k < npend; ++k) {
+    for (int k = narr; k < npend; ++k) {
       const int* r = rec[k];
       const int n = (r[5] - 1) / rg.P - r[4] / rg.P + 1;
-      if ((k == 0 ? old0 : old1) != n - 1) continue;
-      merge_groups<T, D>(p, rg, r[0], r[1], r[2], r[3], r[4], r[5], lane);
-      if (lane == 0) atomicExch(counter(r), 0);
+      if ((k == 0 ? old0 : old1) == n - 1) merge_mask |= 1u << k;
     }
-    npend = 0;
+    narr = npend;
   };
+  // A group has at most two pieces that cross its boundaries (the segments
+  // holding its first and its last unit), and one warp publishes each, so a
+  // warp never holds more than two.
   auto defer_publish = [&](int b, int kvh, int qc, int gc, int seg_lo, int seg_hi) {
-    if (npend == 2) flush_pending();
     if (lane == 0) {
       int* r = pend_rec[kSplit ? 0 : warp][npend];
       r[0] = b;
@@ -1159,10 +1165,10 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
   int st = 0;
   for (int i = 0; i < n_tiles; ++i) {
+    if (!kSplit && narr < npend && issued == n_tiles) arrive_pending();
     const uint32_t sk = stage0 + st * C::kStage;
     const uint32_t sv = sk + C::kKV;
     const uint32_t sq = sk + 2 * C::kKV;
-    if (!kSplit && npend > 0 && issued == n_tiles) flush_pending();
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
       drain_after_timeout<NS>(p.status, bar0, st, phase, issued - i - 1);
@@ -1433,7 +1439,15 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     if (!(fl & kGroupSeg) && !p.post_merge) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
   }
-  if (!kSplit && npend > 0) flush_pending();
+  if (!kSplit && npend > 0) {
+    if (narr < npend) arrive_pending();
+    for (int k = 0; k < npend; ++k) {
+      if (!(merge_mask & (1u << k))) continue;
+      const int* r = pend_rec[kSplit ? 0 : warp][k];
+      merge_groups<T, D>(p, rg, r[0], r[1], r[2], r[3], r[4], r[5], lane);
+      if (lane == 0) atomicExch(pend_counter(r), 0);
+    }
+  }
 }
 
 #if PA_HOST_PART
@@ -2816,7 +2830,16 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
   dim3 merge_grid(1);
   int by_segment = 0, col_split = 0;
   kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment, col_split) ? 1 : 0;
-  kp.snap = (pl.ns == 0 && pl.use_cum && pl.gsz > 1 && !kp.post_merge) ? 1 : 0;
+  // A snapped boundary moves by up to half the longest segment, which one CTA
+  // then streams on top of its share: only worth it while that is about the
+  // cost of the cross-CTA merge it saves (<= 64 KB of K+V, ~1.5 us of one
+  // SM's share of HBM). Long segments (B256 log-uniform 512-32K rows: up to
+  // 1024 tiles moved, +10 % on the step) keep the token-balanced boundaries.
+  const long long seg_bytes = static_cast<long long>(kp.max_nt) * tile * p->head_dim * 4;
+  kp.snap = (pl.ns == 0 && pl.use_cum && pl.gsz > 1 && !kp.post_merge &&
+             seg_bytes <= (128ll << 10))
+                ? 1
+                : 0;
 
   cudaError_t e;
   if (p->dtype == PA_F16)
