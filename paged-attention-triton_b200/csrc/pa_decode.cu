@@ -2176,9 +2176,10 @@ static pa_status_t validate_launch(const pa_decode_params* p) {
 }
 
 // Automatic choice, from B200 sweeps. head_dim 128 (the five benchmark
-// shapes): MHA with pages shorter than 32 tokens, and groups larger than 4
-// query heads, stream best as 16-token tiles on 8 warps; longer pages and 2- or
-// 4-head groups as 32-token tiles on 6 warps. head_dim 64 (128-byte rows):
+// shapes): MHA at every page size, and groups larger than 4 query heads,
+// stream best as 16-token tiles on 8 warps (B1 S4096 page 128: 24.5 -> 22.6 us
+// with L2 flushed; B4 S8192 page 64: 94.6 -> 89.2 us); 2- or 4-head groups as
+// 32-token tiles on 6 warps. head_dim 64 (128-byte rows):
 // MHA as 32-token tiles on 6 warps, query-head groups as 64-token tiles on 6
 // warps. head_dim 256: MHA as 16-token tiles on 5 warps, groups as 32-token
 // tiles on 3 warps.
@@ -2191,7 +2192,7 @@ static int pick_variant(const pa_decode_params* p, bool dup) {
     else if (p->head_dim == 64)
       v = g == 1 ? 3 : 8;   // MHA: 32-token tiles on 6 warps; groups: 64-token tiles
     else
-      v = (!dup || (g == 1 && p->block_size < 32)) ? 5 : 3;
+      v = (!dup || g == 1) ? 5 : 3;
     // 32x6x2 keeps its warps' merge rows in shared memory only up to 2 query
     // columns; with more, and segments that can exceed 8 tiles, 16x8x2 (whose
     // merge rows fit) wins over merging through the workspace.
