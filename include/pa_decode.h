@@ -128,6 +128,9 @@ typedef struct pa_decode_plan_info {
   int32_t generic_path;       /* 1: head_dim 32 or pages not a multiple of 8 tokens: the
                                  CUDA-core split + reduce kernels (kernel_variant 0) */
   size_t workspace_bytes, counter_count;   /* as pa_decode_workspace reports */
+  int32_t cluster_size;       /* CTAs per thread-block cluster (0: no clusters). The device
+                                 may not fit the clusters at once, in which case pa_decode
+                                 falls back to the plain schedule. */
 } pa_decode_plan_info;
 
 PA_API pa_status_t pa_decode_plan(const pa_decode_params* p, pa_decode_plan_info* info);

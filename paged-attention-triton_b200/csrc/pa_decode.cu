@@ -129,6 +129,11 @@ struct KParams {
   // possible segment), so no segment crosses a group and every merge stays in
   // shared memory.
   int snap, max_nt;
+  // Same-length rows, segments longer than a CTA's share: a thread-block
+  // cluster of `clu` CTAs per segment (0: off), each CTA one contiguous part of
+  // it; the CTAs' pieces meet in distributed shared memory (at byte offset
+  // clu_off of every CTA's aligned shared memory) instead of through L2.
+  int clu, clu_off;
 };
 // ----------------------------------------------------------------------------
 // PTX helpers
@@ -211,6 +216,37 @@ __device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
+}
+
+// Distributed shared memory of a thread-block cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_cluster2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr)
+               : "memory");
+  return v;
+}
+// Every thread of every CTA of the cluster arrives; the wait returns once all
+// have (release/acquire: shared-memory writes before the arrival are visible
+// to every CTA after the wait).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 template <typename T>
@@ -776,6 +812,73 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, i
 }
 
 
+// Cluster mode: rank 0 of the cluster merges the CTAs' pieces of its segment
+// (`seg`, in (row, KV head, query chunk) order), reading each CTA's piece rows
+// from that CTA's shared memory; the reference's merge rule
+// (split_kv_kernel.py:101-122). `cslot` is the local shared-memory address of
+// the piece rows ([slot_cols][D + 4] floats, the LSE at D).
+template <typename T, int D, int NW>
+__device__ __forceinline__ void merge_cluster(const KParams& p, uint32_t cslot, int seg, int warp,
+                                              int lane) {
+  constexpr int N = HD<D>::kLaneF;
+  constexpr int kMaxClu = 8;
+  const int per_b = p.Hkv * p.QC;
+  const int b = seg / per_b;
+  const int kvh = (seg - b * per_b) / p.QC;
+  const int qc = seg - b * per_b - kvh * p.QC;
+  const int gc = min(8, p.G - qc * 8);
+  for (int j = warp; j < gc; j += NW) {
+    const uint32_t row = cslot + j * HD<D>::kSlotStride * 4;
+    float l[kMaxClu];
+    RowV<N> v[kMaxClu];
+#pragma unroll
+    for (int k = 0; k < kMaxClu; ++k) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[k].f[i] = 0.f;
+      l[k] = kSentinel;
+      if (k < p.clu) {
+        const uint32_t a = cluster_map(row, k);
+        l[k] = ld_cluster(a + D * 4);
+        const uint32_t ra = a + lane * N * 4;
+        if constexpr (N == 2) {
+          const float2 t = ld_cluster2(ra);
+          v[k].f[0] = t.x;
+          v[k].f[1] = t.y;
+        } else {
+#pragma unroll
+          for (int i = 0; i < N; i += 4) {
+            const float4 t = ld_cluster4(ra + i * 4);
+            v[k].f[i] = t.x;
+            v[k].f[i + 1] = t.y;
+            v[k].f[i + 2] = t.z;
+            v[k].f[i + 3] = t.w;
+          }
+        }
+      }
+    }
+    float gmax = kValidLse;
+#pragma unroll
+    for (int k = 0; k < kMaxClu; ++k)
+      if (l[k] > kValidLse) gmax = fmaxf(gmax, l[k]);
+    float gsum = 0.f;
+    RowV<N> a;
+#pragma unroll
+    for (int i = 0; i < N; ++i) a.f[i] = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxClu; ++k) {
+      const float wgt = (l[k] > kValidLse) ? exp2f((l[k] - gmax) * kLog2e) : 0.f;
+      gsum += wgt;
+#pragma unroll
+      for (int i = 0; i < N; ++i) a.f[i] = fmaf(wgt, v[k].f[i], a.f[i]);
+    }
+    const float inv = __fdividef(1.f, fmaxf(gsum, 1e-20f));
+#pragma unroll
+    for (int i = 0; i < N; ++i) a.f[i] *= inv;
+    store_out<T, D>(p, b, kvh * p.G + qc * 8 + j, lane, a,
+                    gsum > 0.f ? gmax + __logf(gsum) : kSentinel);
+  }
+}
+
 // Cold paths, out of line so that the hot path's straight-line code does not
 // interleave with them (the short steps are bound by instruction fetch).
 
@@ -834,6 +937,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   float* gslots = p.wslots ? p.wslots + static_cast<size_t>(blockIdx.x) * NW * 2 * p.slot_cols *
                                             H::kSlotStride
                            : reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
+  // Cluster mode: this CTA's piece of its segment, read by the cluster's rank 0.
+  float* cslot = (!kSplit && !kCum && p.clu) ? reinterpret_cast<float*>(smem + p.clu_off) : nullptr;
   __shared__ int warp_tot[NW];
   // Cross-group publishes waiting until the warp has issued all its copies:
   // [warp][2 entries][b, kvh, qc, gc, seg_lo, seg_hi].
@@ -873,7 +978,22 @@ __global__ void __launch_bounds__(NW * 32, 1)
     rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
   };
   // Same-length rows: the ranges need no memory, so they are set before the wait.
-  if (!kSplit && !kCum) set_ranges(p.U, p.P, p.Pw);
+  if (!kSplit && !kCum) {
+    set_ranges(p.U, p.P, p.Pw);
+    if (p.clu) {
+      // cluster c owns segment c; its CTA of rank r the units
+      // [r * P, (r + 1) * P) of that segment (the host sizes P so that every
+      // rank has some)
+      uint32_t cid, crank;
+      asm("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
+      asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+      const int s0 = static_cast<int>(cid) * p.nt_u;
+      rg.gr0 = s0 + static_cast<int>(crank) * p.P;
+      rg.gr1 = min(rg.gr0 + p.P, s0 + p.nt_u);
+      rg.wr0 = min(rg.gr1, rg.gr0 + rg.gi * rg.Pw);
+      rg.wr1 = min(rg.gr1, rg.wr0 + rg.Pw);
+    }
+  }
 
   // Programmatic dependent launch: everything above touches no global memory;
   // from here on the kernel reads inputs (and writes outputs, partials and
@@ -1172,6 +1292,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
       drain_after_timeout<NS>(p.status, bar0, st, phase, issued - i - 1);
+      if (cslot) break;   // every thread of a cluster reaches its barriers
       return;
     }
     phase ^= 1u << st;
@@ -1382,8 +1503,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
           od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * H::kSlotStride;
           ld = od + D;
         } else if (!kSplit) {
-          od = gslot_row<D>(p, gslot, c);
-          ld = gslot_lse(p, gslot, c);
+          od = cslot ? cslot + c * H::kSlotStride : gslot_row<D>(p, gslot, c);
+          ld = cslot ? od + D : gslot_lse(p, gslot, c);
         } else {
           const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + w.s;
           od = p.o_part + row * D;
@@ -1409,7 +1530,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       continue;
     }
     if (dest == 1) {
-      if (!p.post_merge) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
+      if (!p.post_merge && !cslot) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
       continue;
     }
 
@@ -1432,12 +1553,15 @@ __global__ void __launch_bounds__(NW * 32, 1)
       merge_rows_smem<D>(nw, lane, src, o4, lse);
       if (fl & kGroupSeg) {
         store_out<T, D>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
+      } else if (cslot) {
+        store_row(cslot + j * H::kSlotStride, lane, o4);
+        if (lane == 0) cslot[j * H::kSlotStride + D] = lse;
       } else {
         store_row(gslot_row<D>(p, gslot, j), lane, o4);
         if (lane == 0) *gslot_lse(p, gslot, j) = lse;
       }
     }
-    if (!(fl & kGroupSeg) && !p.post_merge) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
+    if (!(fl & kGroupSeg) && !p.post_merge && !cslot) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
   }
   if (!kSplit && npend > 0) {
     if (narr < npend) arrive_pending();
@@ -1446,6 +1570,22 @@ __global__ void __launch_bounds__(NW * 32, 1)
       const int* r = pend_rec[kSplit ? 0 : warp][k];
       merge_groups<T, D>(p, rg, r[0], r[1], r[2], r[3], r[4], r[5], lane);
       if (lane == 0) atomicExch(pend_counter(r), 0);
+    }
+  }
+  if constexpr (!kSplit && !kCum) {
+    if (cslot) {
+      // Every CTA's piece is in its shared memory once the cluster barrier
+      // completes (each thread arrives after finite, bounded waits); rank 0
+      // merges them, and the second barrier keeps every CTA's shared memory
+      // alive until it has.
+      __syncwarp();
+      cluster_sync_all();
+      uint32_t crank, cid;
+      asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+      asm("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
+      if (crank == 0) merge_cluster<T, D, NW>(p, smem_u32(cslot), static_cast<int>(cid), warp, lane);
+      __syncwarp();
+      cluster_sync_all();
     }
   }
 }
@@ -2081,6 +2221,8 @@ struct Plan {
   size_t ws_bytes = 0;
   size_t counters = 0;
   bool generic = false;    // the CUDA-core split + reduce path (uncommon shapes)
+  int clu = 0;             // balanced, same length: CTAs per thread-block cluster (0: none)
+  int clu_off = 0;         // cluster mode: shared-memory offset of the CTA's piece rows
 };
 
 // Shapes the TMA tile kernels do not cover: head_dim 32, or pages that are not
@@ -2214,7 +2356,66 @@ static size_t group_slot_bytes(const Plan& pl, size_t slots) {
   return (b + 15) & ~size_t(15);
 }
 
-static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
+// Cluster mode (same-length rows, whole-CTA groups whose merge rows are in
+// shared memory, segments longer than a CTA's share): one cluster of `clu`
+// CTAs per segment, clu = min(8, sms / segments) >= 2, used when the clusters
+// still cover >= 3/4 of the SMs. The CTAs' pieces meet in distributed shared
+// memory at the end of the kernel instead of through L2 arrivals and a merge
+// by the last CTA (B1 H32 S4096, page 128: the cross-CTA tail of ~3.5 us).
+// Cluster launches the device could not hold at once (cudaOccupancyMaxActiveClusters),
+// so that later calls plan without clusters directly.
+struct CluBad { int dev, variant, D, dup, dtype, clu, smem; };
+static CluBad g_clu_bad[32];
+static int g_nclu_bad = 0;
+
+static bool cluster_known_bad(const CluBad& k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int i = 0; i < g_nclu_bad; ++i) {
+    const CluBad& e = g_clu_bad[i];
+    if (e.dev == k.dev && e.variant == k.variant && e.D == k.D && e.dup == k.dup &&
+        e.dtype == k.dtype && e.clu == k.clu && e.smem == k.smem)
+      return true;
+  }
+  return false;
+}
+
+static void cluster_mark_bad(const CluBad& k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_nclu_bad < 32) g_clu_bad[g_nclu_bad++] = k;
+}
+
+static CluBad cluster_key(const pa_decode_params* p, const Plan& pl) {
+  return CluBad{current_device(), pl.variant, pl.D, pl.dup ? 1 : 0, p->dtype, pl.clu, pl.smem};
+}
+
+static void plan_cluster(const pa_decode_params* p, int sms, Plan& pl) {
+  if (pl.ns != 0 || pl.use_cum || pl.gsz == 1 || pl.wslot_global || p->seq_len <= 0) return;
+  const Variant& v = kVariants[pl.variant - 1];
+  const long long nseg = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
+  const long long nt = (p->seq_len + v.tile - 1) / v.tile;
+  if (nseg < 1 || 2 * nseg > sms) return;
+  const int clu = static_cast<int>(std::min<long long>(8, sms / nseg));
+  if (clu < 2 || 4 * nseg * clu < 3ll * sms) return;
+  // only where the plain schedule splits segments between CTAs
+  const long long groups = pl.W / pl.gsz;
+  if (std::max<long long>((nseg * nt + groups - 1) / groups, pl.gsz) >= nt) return;
+  const long long per = (nt + clu - 1) / clu;   // units per CTA
+  if ((clu - 1) * per >= nt) return;            // every rank has units
+  const long long off = (static_cast<long long>(pl.smem) - 1024 + 15) & ~15ll;
+  const long long bytes = static_cast<long long>(pl.slot_cols) * (pl.D + 4) * 4;
+  if (off + bytes + 1024 > kMaxSmem) return;
+  Plan c = pl;
+  c.clu = clu;
+  c.clu_off = static_cast<int>(off);
+  c.smem = static_cast<int>(off + bytes + 1024);
+  c.grid = static_cast<int>(nseg) * clu;
+  c.W = c.grid * v.nw;
+  if (cluster_known_bad(cluster_key(p, c))) return;
+  pl = c;
+}
+
+static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl,
+                             bool allow_cluster = true) {
   pl.G = p->num_heads / p->num_kv_heads;
   pl.QC = (pl.G + 7) / 8;
   pl.dup = (pl.G == 1 || pl.G == 2 || pl.G == 4);
@@ -2301,6 +2502,7 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl) {
     pl.ws_bytes = (p->o_partial && p->lse_partial) ? 0 : rows * (pl.D + 1) * sizeof(float);
   }
   pl.counters = static_cast<size_t>(p->batch) * nseg;
+  if (allow_cluster) plan_cluster(p, sms, pl);
   return PA_OK;
 }
 
@@ -2410,7 +2612,7 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   // previous kernel in the stream finishes; the kernel's griddepcontrol.wait
   // orders all of its memory accesses after that kernel.
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(pl.grid);
@@ -2419,6 +2621,34 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (pl.clu) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = pl.clu;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    // Every cluster must be resident at once (one CTA per SM): checked once
+    // per device, cluster size and shared-memory size.
+    struct Seen { int dev, clu, smem, ok; };
+    static Seen seen[16];
+    static int nseen = 0;
+    int ok = -1;
+    {
+      std::lock_guard<std::mutex> lk(mu);
+      for (int i = 0; i < nseen; ++i)
+        if (seen[i].dev == dev && seen[i].clu == pl.clu && seen[i].smem == pl.smem) ok = seen[i].ok;
+    }
+    if (ok < 0) {
+      int n = 0;
+      const cudaError_t q = cudaOccupancyMaxActiveClusters(
+          &n, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>, &cfg);
+      ok = (q == cudaSuccess && n * pl.clu >= pl.grid) ? 1 : 0;
+      if (q != cudaSuccess) (void)cudaGetLastError();
+      std::lock_guard<std::mutex> lk(mu);
+      if (nseen < 16) seen[nseen++] = Seen{dev, pl.clu, pl.smem, ok};
+    }
+    if (!ok) return cudaErrorCooperativeLaunchTooLarge;   // the caller re-plans without clusters
+  }
   return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>, mk, mv, kp);
 }
 
@@ -2677,6 +2907,12 @@ static void build_kparams(const pa_decode_params* p, const Plan& pl, KParams& kp
   kp.div_bs = make_fastdiv(static_cast<uint32_t>(p->block_size));
   const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
   kp.max_nt = static_cast<int>(std::min<long long>((cap + tile - 1) / tile, 0x3fffffff));
+  if (pl.clu) {
+    kp.clu = pl.clu;
+    kp.clu_off = pl.clu_off;
+    kp.P = (kp.nt_u + pl.clu - 1) / pl.clu;
+    kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
+  }
 }
 
 // Whether the segments that cross group boundaries merge in
@@ -2691,7 +2927,7 @@ static void build_kparams(const pa_decode_params* p, const Plan& pl, KParams& kp
 // Single-warp groups over long segments (pl.long_pieces) always take the pass.
 static bool want_post_merge(const pa_decode_params* p, const Plan& pl, const KParams& kp,
                             dim3& grid, int& by_segment, int& col_split) {
-  if (pl.ns != 0 || (pl.gsz == 1 && !pl.long_pieces)) return false;
+  if (pl.ns != 0 || pl.clu || (pl.gsz == 1 && !pl.long_pieces)) return false;
   const int ngroups = pl.W / pl.gsz;
   if (ngroups < 2) return false;
   const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
@@ -2799,6 +3035,7 @@ pa_status_t pa_decode_plan(const pa_decode_params* p, pa_decode_plan_info* info)
   info->smem_bytes = pl.smem;
   info->workspace_bytes = pl.ws_bytes;
   info->counter_count = pl.counters;
+  info->cluster_size = pl.clu;
   return PA_OK;
 }
 
@@ -2842,13 +3079,24 @@ pa_status_t pa_decode(const pa_decode_params* p, cudaStream_t stream) {
                 ? 1
                 : 0;
 
-  cudaError_t e;
-  if (p->dtype == PA_F16)
-    e = pl.dup ? launch<__half, true>(pl, mk, mv, kp, stream, dev)
-               : launch<__half, false>(pl, mk, mv, kp, stream, dev);
-  else
-    e = pl.dup ? launch<__nv_bfloat16, true>(pl, mk, mv, kp, stream, dev)
-               : launch<__nv_bfloat16, false>(pl, mk, mv, kp, stream, dev);
+  auto launch_decode = [&]() {
+    if (p->dtype == PA_F16)
+      return pl.dup ? launch<__half, true>(pl, mk, mv, kp, stream, dev)
+                    : launch<__half, false>(pl, mk, mv, kp, stream, dev);
+    return pl.dup ? launch<__nv_bfloat16, true>(pl, mk, mv, kp, stream, dev)
+                  : launch<__nv_bfloat16, false>(pl, mk, mv, kp, stream, dev);
+  };
+  cudaError_t e = launch_decode();
+  if (e == cudaErrorCooperativeLaunchTooLarge && pl.clu) {
+    // the clusters cannot all be resident on this device: the plain schedule
+    cluster_mark_bad(cluster_key(p, pl));
+    pl = Plan();
+    s = make_plan(p, sms, pl, false);
+    if (s != PA_OK) return s;
+    build_kparams(p, pl, kp);
+    kp.post_merge = want_post_merge(p, pl, kp, merge_grid, by_segment, col_split) ? 1 : 0;
+    e = launch_decode();
+  }
   if (e == cudaSuccess && kp.post_merge) {
     MergeParams m;
     memset(&m, 0, sizeof(m));

@@ -120,6 +120,7 @@ class PlanInfo(ctypes.Structure):
         ("generic_path", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_size_t),
         ("counter_count", ctypes.c_size_t),
+        ("cluster_size", ctypes.c_int32),
     ]
 
 
