@@ -917,7 +917,8 @@ __device__ __noinline__ void zero_length_rows(int B, int Hq, char* out, long lon
 // ----------------------------------------------------------------------------
 // Kernel
 // ----------------------------------------------------------------------------
-template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum,
+          bool kClu>
 __global__ void __launch_bounds__(NW * 32, 1)
     pa_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const KParams p) {
@@ -938,7 +939,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
                                             H::kSlotStride
                            : reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
   // Cluster mode: this CTA's piece of its segment, read by the cluster's rank 0.
-  float* cslot = (!kSplit && !kCum && p.clu) ? reinterpret_cast<float*>(smem + p.clu_off) : nullptr;
+  float* cslot = kClu ? reinterpret_cast<float*>(smem + p.clu_off) : nullptr;
   __shared__ int warp_tot[NW];
   // Cross-group publishes waiting until the warp has issued all its copies:
   // [warp][2 entries][b, kvh, qc, gc, seg_lo, seg_hi].
@@ -980,7 +981,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // Same-length rows: the ranges need no memory, so they are set before the wait.
   if (!kSplit && !kCum) {
     set_ranges(p.U, p.P, p.Pw);
-    if (p.clu) {
+    if constexpr (kClu) {
       // cluster c owns segment c; its CTA of rank r the units
       // [r * P, (r + 1) * P) of that segment (the host sizes P so that every
       // rank has some)
@@ -1572,8 +1573,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (lane == 0) atomicExch(pend_counter(r), 0);
     }
   }
-  if constexpr (!kSplit && !kCum) {
-    if (cslot) {
+  if constexpr (kClu) {
+    {
       // Every CTA's piece is in its shared memory once the cluster barrier
       // completes (each thread arrives after finite, bounded waits); rank 0
       // merges them, and the second barrier keeps every CTA's shared memory
@@ -2591,7 +2592,8 @@ static bool cached_cache_map(CUtensorMap* map, const pa_decode_params* p, int de
 
 #endif  // PA_HOST_PART
 
-template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum>
+template <typename T, bool kDup, int TILE, int NW, int NS, int D, bool kSplit, bool kCum,
+          bool kClu>
 cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                           const KParams& kp, cudaStream_t stream, int dev) {
   using C = Cfg<kDup, TILE, NW, NS, D>;
@@ -2601,7 +2603,7 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!attr_set[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>,
+      const cudaError_t e = cudaFuncSetAttribute(pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum, kClu>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kMaxSmem);
       if (e != cudaSuccess) return e;
@@ -2621,7 +2623,7 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (pl.clu) {
+  if (kClu) {
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = pl.clu;
     attr[1].val.clusterDim.y = 1;
@@ -2641,7 +2643,7 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
     if (ok < 0) {
       int n = 0;
       const cudaError_t q = cudaOccupancyMaxActiveClusters(
-          &n, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>, &cfg);
+          &n, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum, kClu>, &cfg);
       ok = (q == cudaSuccess && n * pl.clu >= pl.grid) ? 1 : 0;
       if (q != cudaSuccess) (void)cudaGetLastError();
       std::lock_guard<std::mutex> lk(mu);
@@ -2649,18 +2651,19 @@ cudaError_t launch_kernel(const Plan& pl, const CUtensorMap& mk, const CUtensorM
     }
     if (!ok) return cudaErrorCooperativeLaunchTooLarge;   // the caller re-plans without clusters
   }
-  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum>, mk, mv, kp);
+  return cudaLaunchKernelEx(&cfg, pa_decode_kernel<T, kDup, TILE, NW, NS, D, kSplit, kCum, kClu>, mk, mv, kp);
 }
 
 // Every decode kernel the dispatch below can launch, as (variant, layout) per
 // head_dim and dtype; PFX is `extern` for declarations, empty for definitions.
-#define PA_LK(T, DUP, TILE, NW, NS, D, SPLIT, CUM)                                          \
-  cudaError_t launch_kernel<T, DUP, TILE, NW, NS, D, SPLIT, CUM>(                           \
+#define PA_LK(T, DUP, TILE, NW, NS, D, SPLIT, CUM, CLU)                                     \
+  cudaError_t launch_kernel<T, DUP, TILE, NW, NS, D, SPLIT, CUM, CLU>(                      \
       const Plan&, const CUtensorMap&, const CUtensorMap&, const KParams&, cudaStream_t, int)
-#define PA_BOTH(PFX, T, DUP, TILE, NW, NS, D)                 \
-  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, false);  \
-  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, true);   \
-  PFX template PA_LK(T, DUP, TILE, NW, NS, D, true, false);
+#define PA_BOTH(PFX, T, DUP, TILE, NW, NS, D)                        \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, false, false);  \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, false, true);   \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, false, true, false);   \
+  PFX template PA_LK(T, DUP, TILE, NW, NS, D, true, false, false);
 #define PA_D128(PFX, T)                                                              \
   PA_BOTH(PFX, T, true, 32, 4, 3, 128) PA_BOTH(PFX, T, false, 32, 4, 3, 128)         \
   PA_BOTH(PFX, T, true, 16, 8, 3, 128)                                               \
@@ -2688,17 +2691,20 @@ PA_D256(extern, __half)
 PA_D256(extern, __nv_bfloat16)
 #endif
 
-// The split schedule, the balanced schedule over same-length rows and the
-// balanced schedule over per-row lengths are separate kernels: none carries
-// another's code (short steps are bound by instruction fetch).
+// The split schedule, the balanced schedule over same-length rows (plain, or
+// as thread-block clusters) and the balanced schedule over per-row lengths are
+// separate kernels: none carries another's code (short steps are bound by
+// instruction fetch).
 template <typename T, bool kDup, int TILE, int NW, int NS, int D>
 static cudaError_t launch_one(const Plan& pl, const CUtensorMap& mk, const CUtensorMap& mv,
                               const KParams& kp, cudaStream_t stream, int dev) {
   if (pl.ns != 0)
-    return launch_kernel<T, kDup, TILE, NW, NS, D, true, false>(pl, mk, mv, kp, stream, dev);
+    return launch_kernel<T, kDup, TILE, NW, NS, D, true, false, false>(pl, mk, mv, kp, stream, dev);
   if (pl.use_cum)
-    return launch_kernel<T, kDup, TILE, NW, NS, D, false, true>(pl, mk, mv, kp, stream, dev);
-  return launch_kernel<T, kDup, TILE, NW, NS, D, false, false>(pl, mk, mv, kp, stream, dev);
+    return launch_kernel<T, kDup, TILE, NW, NS, D, false, true, false>(pl, mk, mv, kp, stream, dev);
+  if (pl.clu)
+    return launch_kernel<T, kDup, TILE, NW, NS, D, false, false, true>(pl, mk, mv, kp, stream, dev);
+  return launch_kernel<T, kDup, TILE, NW, NS, D, false, false, false>(pl, mk, mv, kp, stream, dev);
 }
 
 template <typename T, bool kDup>
