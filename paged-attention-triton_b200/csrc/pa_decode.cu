@@ -821,7 +821,6 @@ template <typename T, int D, int NW>
 __device__ __forceinline__ void merge_cluster(const KParams& p, uint32_t cslot, int seg, int warp,
                                               int lane) {
   constexpr int N = HD<D>::kLaneF;
-  constexpr int kMaxClu = 8;
   const int per_b = p.Hkv * p.QC;
   const int b = seg / per_b;
   const int kvh = (seg - b * per_b) / p.QC;
@@ -829,53 +828,47 @@ __device__ __forceinline__ void merge_cluster(const KParams& p, uint32_t cslot, 
   const int gc = min(8, p.G - qc * 8);
   for (int j = warp; j < gc; j += NW) {
     const uint32_t row = cslot + j * HD<D>::kSlotStride * 4;
-    float l[kMaxClu];
-    RowV<N> v[kMaxClu];
-#pragma unroll
-    for (int k = 0; k < kMaxClu; ++k) {
-#pragma unroll
-      for (int i = 0; i < N; ++i) v[k].f[i] = 0.f;
-      l[k] = kSentinel;
-      if (k < p.clu) {
-        const uint32_t a = cluster_map(row, k);
-        l[k] = ld_cluster(a + D * 4);
-        const uint32_t ra = a + lane * N * 4;
-        if constexpr (N == 2) {
-          const float2 t = ld_cluster2(ra);
-          v[k].f[0] = t.x;
-          v[k].f[1] = t.y;
-        } else {
-#pragma unroll
-          for (int i = 0; i < N; i += 4) {
-            const float4 t = ld_cluster4(ra + i * 4);
-            v[k].f[i] = t.x;
-            v[k].f[i + 1] = t.y;
-            v[k].f[i + 2] = t.z;
-            v[k].f[i + 3] = t.w;
-          }
-        }
-      }
-    }
-    float gmax = kValidLse;
-#pragma unroll
-    for (int k = 0; k < kMaxClu; ++k)
-      if (l[k] > kValidLse) gmax = fmaxf(gmax, l[k]);
-    float gsum = 0.f;
+    // One compact loop with a running max (the order of split_kv_kernel.py:105-118):
+    // this code runs once per step, on its critical path, where unrolled code is
+    // paid for in instruction fetch; a distributed-shared-memory load is short.
+    float m = kValidLse, sum = 0.f;
     RowV<N> a;
 #pragma unroll
     for (int i = 0; i < N; ++i) a.f[i] = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < p.clu; ++k) {
+      const uint32_t ra = cluster_map(row, k);
+      const float l = ld_cluster(ra + D * 4);
+      RowV<N> v;
+      const uint32_t la = ra + lane * N * 4;
+      if constexpr (N == 2) {
+        const float2 t = ld_cluster2(la);
+        v.f[0] = t.x;
+        v.f[1] = t.y;
+      } else {
 #pragma unroll
-    for (int k = 0; k < kMaxClu; ++k) {
-      const float wgt = (l[k] > kValidLse) ? exp2f((l[k] - gmax) * kLog2e) : 0.f;
-      gsum += wgt;
+        for (int i = 0; i < N; i += 4) {
+          const float4 t = ld_cluster4(la + i * 4);
+          v.f[i] = t.x;
+          v.f[i + 1] = t.y;
+          v.f[i + 2] = t.z;
+          v.f[i + 3] = t.w;
+        }
+      }
+      if (l > kValidLse) {
+        const float mn = fmaxf(m, l);
+        const float f = exp2f((m - mn) * kLog2e);
+        const float wgt = exp2f((l - mn) * kLog2e);
+        sum = fmaf(sum, f, wgt);
 #pragma unroll
-      for (int i = 0; i < N; ++i) a.f[i] = fmaf(wgt, v[k].f[i], a.f[i]);
+        for (int i = 0; i < N; ++i) a.f[i] = fmaf(a.f[i], f, wgt * v.f[i]);
+        m = mn;
+      }
     }
-    const float inv = __fdividef(1.f, fmaxf(gsum, 1e-20f));
+    const float inv = __fdividef(1.f, fmaxf(sum, 1e-20f));
 #pragma unroll
     for (int i = 0; i < N; ++i) a.f[i] *= inv;
-    store_out<T, D>(p, b, kvh * p.G + qc * 8 + j, lane, a,
-                    gsum > 0.f ? gmax + __logf(gsum) : kSentinel);
+    store_out<T, D>(p, b, kvh * p.G + qc * 8 + j, lane, a, sum > 0.f ? m + __logf(sum) : kSentinel);
   }
 }
 
