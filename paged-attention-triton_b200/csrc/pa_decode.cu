@@ -224,29 +224,26 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_cluster(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
-__device__ __forceinline__ float4 ld_cluster4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ float2 ld_cluster2(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr)
+// One thread's arrival on an mbarrier in another CTA of the cluster; its
+// earlier stores to that CTA's shared memory are visible to whoever completes
+// a wait on the barrier's phase with cluster-scope acquire.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
                : "memory");
-  return v;
 }
-// Every thread of every CTA of the cluster arrives; the wait returns once all
-// have (release/acquire: shared-memory writes before the arrival are visible
-// to every CTA after the wait).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
 template <typename T>
@@ -812,50 +809,47 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int b, int kvh, i
 }
 
 
-// Cluster mode: rank 0 of the cluster merges the CTAs' pieces of its segment
-// (`seg`, in (row, KV head, query chunk) order), reading each CTA's piece rows
-// from that CTA's shared memory; the reference's merge rule
-// (split_kv_kernel.py:101-122). `cslot` is the local shared-memory address of
-// the piece rows ([slot_cols][D + 4] floats, the LSE at D).
+// Cluster mode, rank 0 of the cluster: once every CTA of the cluster has
+// pushed its piece of the segment (`seg`, in (row, KV head, query chunk)
+// order) into this CTA's shared memory (`crow`: [clu][slot_cols][D + 4]
+// floats, the LSE at D) and arrived on `cbar`, merge the pieces with the
+// reference's rule (split_kv_kernel.py:101-122) and write O and LSE. The wait
+// is bounded (four times a copy wait, as a pushing CTA may itself have waited
+// out one): on timeout the status word gets PA_STATUS_TIMEOUT and nothing is
+// written.
 template <typename T, int D, int NW>
-__device__ __forceinline__ void merge_cluster(const KParams& p, uint32_t cslot, int seg, int warp,
-                                              int lane) {
+__device__ __forceinline__ void merge_cluster(const KParams& p, const float* crow, uint32_t cbar,
+                                              int seg, int warp, int lane) {
   constexpr int N = HD<D>::kLaneF;
   const int per_b = p.Hkv * p.QC;
   const int b = seg / per_b;
   const int kvh = (seg - b * per_b) / p.QC;
   const int qc = seg - b * per_b - kvh * p.QC;
   const int gc = min(8, p.G - qc * 8);
+  if (warp >= gc) return;
+  if (!mbar_try_wait_cluster(cbar, 0)) {
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait_cluster(cbar, 0)) {
+      if (global_ns() - t0 > 4 * kWaitLimitNs) {
+        if (lane == 0 && p.status) atomicOr(p.status, PA_STATUS_TIMEOUT);
+        return;
+      }
+    }
+  }
   for (int j = warp; j < gc; j += NW) {
-    const uint32_t row = cslot + j * HD<D>::kSlotStride * 4;
     // One compact loop with a running max (the order of split_kv_kernel.py:105-118):
     // this code runs once per step, on its critical path, where unrolled code is
-    // paid for in instruction fetch; a distributed-shared-memory load is short.
+    // paid for in instruction fetch.
     float m = kValidLse, sum = 0.f;
     RowV<N> a;
 #pragma unroll
     for (int i = 0; i < N; ++i) a.f[i] = 0.f;
 #pragma unroll 1
     for (int k = 0; k < p.clu; ++k) {
-      const uint32_t ra = cluster_map(row, k);
-      const float l = ld_cluster(ra + D * 4);
-      RowV<N> v;
-      const uint32_t la = ra + lane * N * 4;
-      if constexpr (N == 2) {
-        const float2 t = ld_cluster2(la);
-        v.f[0] = t.x;
-        v.f[1] = t.y;
-      } else {
-#pragma unroll
-        for (int i = 0; i < N; i += 4) {
-          const float4 t = ld_cluster4(la + i * 4);
-          v.f[i] = t.x;
-          v.f[i + 1] = t.y;
-          v.f[i + 2] = t.z;
-          v.f[i + 3] = t.w;
-        }
-      }
+      const float* row = crow + (k * p.slot_cols + j) * HD<D>::kSlotStride;
+      const float l = row[D];
       if (l > kValidLse) {
+        const RowV<N> v = load_row<false, N>(row, lane);
         const float mn = fmaxf(m, l);
         const float f = exp2f((m - mn) * kLog2e);
         const float wgt = exp2f((l - mn) * kLog2e);
@@ -931,8 +925,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
   float* gslots = p.wslots ? p.wslots + static_cast<size_t>(blockIdx.x) * NW * 2 * p.slot_cols *
                                             H::kSlotStride
                            : reinterpret_cast<float*>(smem + C::kGroupOff + C::kGroupCntBytes);
-  // Cluster mode: this CTA's piece of its segment, read by the cluster's rank 0.
-  float* cslot = kClu ? reinterpret_cast<float*>(smem + p.clu_off) : nullptr;
+  // Cluster mode: rank 0's arrival barrier for the CTAs' pieces (cbar), then
+  // the pieces themselves ([clu][slot_cols][D + 4] floats; every CTA carves
+  // the same layout, only rank 0's is used). crank / cid: this CTA's rank in
+  // its cluster and the cluster's index, which is its segment.
+  float* cslot = kClu ? reinterpret_cast<float*>(smem + p.clu_off + 16) : nullptr;
+  const uint32_t cbar = kClu ? smem_u32(smem + p.clu_off) : 0u;
+  uint32_t crank = 0, cid = 0;
+  if constexpr (kClu) {
+    asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+    asm("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
+  }
   __shared__ int warp_tot[NW];
   // Cross-group publishes waiting until the warp has issued all its copies:
   // [warp][2 entries][b, kvh, qc, gc, seg_lo, seg_hi].
@@ -954,6 +957,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // copy; the CTA-wide barrier that publishes gcnt comes after the first
   // copies are in flight.
   __syncwarp();
+  if constexpr (kClu) {
+    // One arrival per lane of each CTA's pushing warp. The cluster barrier's
+    // arrive here and wait after the first copies make the initialisation
+    // visible to every CTA before any of them can push.
+    if (threadIdx.x == 0) {
+      mbar_init(cbar, static_cast<uint32_t>(p.clu) * 32u);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  }
 
   // ---------------------------------------------------------------- schedule
   const int wid = blockIdx.x * NW + warp;
@@ -978,9 +992,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
       // cluster c owns segment c; its CTA of rank r the units
       // [r * P, (r + 1) * P) of that segment (the host sizes P so that every
       // rank has some)
-      uint32_t cid, crank;
-      asm("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
-      asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
       const int s0 = static_cast<int>(cid) * p.nt_u;
       rg.gr0 = s0 + static_cast<int>(crank) * p.P;
       rg.gr1 = min(rg.gr0 + p.P, s0 + p.nt_u);
@@ -1185,6 +1196,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // first batch has no second one).
   if (u0n < u1n) batch_pages<TILE, kSplit, kCum>(p, cum, rg, w, u0n, u1n, lane, pg_n, sl_n);
   if (!kSplit) __syncthreads();   // gcnt is zero for every warp's merges
+  if constexpr (kClu) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   // The next kernel in the stream may start its own prologue on SMs this grid
   // leaves; it waits for this grid's completion before touching memory.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1286,7 +1298,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 
     if (!mbar_wait(bar0 + st * 8, (phase >> st) & 1)) {
       drain_after_timeout<NS>(p.status, bar0, st, phase, issued - i - 1);
-      if (cslot) break;   // every thread of a cluster reaches its barriers
+      if (kClu) break;   // rank 0's merging warps still wait (bounded) for every push
       return;
     }
     phase ^= 1u << st;
@@ -1490,6 +1502,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
               Mma<T>::from_float(o[md][e + 2] * inv_l);
         }
         if (rr == 0 && p.lse) p.lse[b * p.Hq + hq] = lse;
+      } else if (kClu && dest == 1) {
+        // the CTA's piece, straight into rank 0's shared memory
+        const uint32_t r =
+            cluster_map(smem_u32(cslot + (crank * p.slot_cols + c) * H::kSlotStride), 0);
+#pragma unroll
+        for (int md = 0; md < H::kSteps; ++md) {
+          const int d0i = md * 16 + rr;
+          st_cluster(r + d0i * 4, o[md][e] * inv_l);
+          st_cluster(r + (d0i + 8) * 4, o[md][e + 2] * inv_l);
+        }
+        if (rr == 0) st_cluster(r + D * 4, lse);
       } else {
         float* od;
         float* ld;
@@ -1497,8 +1520,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
           od = gslots + ((rg.gi * 2 + wside) * p.slot_cols + c) * H::kSlotStride;
           ld = od + D;
         } else if (!kSplit) {
-          od = cslot ? cslot + c * H::kSlotStride : gslot_row<D>(p, gslot, c);
-          ld = cslot ? od + D : gslot_lse(p, gslot, c);
+          od = gslot_row<D>(p, gslot, c);
+          ld = gslot_lse(p, gslot, c);
         } else {
           const long long row = (static_cast<long long>(b) * p.Hq + hq) * p.ns + w.s;
           od = p.o_part + row * D;
@@ -1524,7 +1547,10 @@ __global__ void __launch_bounds__(NW * 32, 1)
       continue;
     }
     if (dest == 1) {
-      if (!p.post_merge && !cslot) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
+      if constexpr (kClu)
+        mbar_arrive_cluster(cluster_map(cbar, 0));
+      else if (!p.post_merge)
+        defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
       continue;
     }
 
@@ -1547,15 +1573,21 @@ __global__ void __launch_bounds__(NW * 32, 1)
       merge_rows_smem<D>(nw, lane, src, o4, lse);
       if (fl & kGroupSeg) {
         store_out<T, D>(p, b, kvh * G + qc * 8 + j, lane, o4, lse);
-      } else if (cslot) {
-        store_row(cslot + j * H::kSlotStride, lane, o4);
-        if (lane == 0) cslot[j * H::kSlotStride + D] = lse;
+      } else if (kClu) {
+        const uint32_t r =
+            cluster_map(smem_u32(cslot + (crank * p.slot_cols + j) * H::kSlotStride), 0);
+#pragma unroll
+        for (int i = 0; i < H::kLaneF; ++i) st_cluster(r + (lane * H::kLaneF + i) * 4, o4.f[i]);
+        if (lane == 0) st_cluster(r + D * 4, lse);
       } else {
         store_row(gslot_row<D>(p, gslot, j), lane, o4);
         if (lane == 0) *gslot_lse(p, gslot, j) = lse;
       }
     }
-    if (!(fl & kGroupSeg) && !p.post_merge && !cslot) defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
+    if constexpr (kClu)
+      mbar_arrive_cluster(cluster_map(cbar, 0));
+    else if (!(fl & kGroupSeg) && !p.post_merge)
+      defer_publish(b, kvh, qc, gc, seg_lo, seg_hi);
   }
   if (!kSplit && npend > 0) {
     if (narr < npend) arrive_pending();
@@ -1567,20 +1599,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
   }
   if constexpr (kClu) {
-    {
-      // Every CTA's piece is in its shared memory once the cluster barrier
-      // completes (each thread arrives after finite, bounded waits); rank 0
-      // merges them, and the second barrier keeps every CTA's shared memory
-      // alive until it has.
-      __syncwarp();
-      cluster_sync_all();
-      uint32_t crank, cid;
-      asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
-      asm("mov.u32 %0, %%clusterid.x;" : "=r"(cid));
-      if (crank == 0) merge_cluster<T, D, NW>(p, smem_u32(cslot), static_cast<int>(cid), warp, lane);
-      __syncwarp();
-      cluster_sync_all();
-    }
+    // Rank 0 stays resident until every CTA's piece has landed in its shared
+    // memory (the other CTAs only write there and may exit at once).
+    if (crank == 0) merge_cluster<T, D, NW>(p, cslot, cbar, static_cast<int>(cid), warp, lane);
   }
 }
 
@@ -2396,7 +2417,8 @@ static void plan_cluster(const pa_decode_params* p, int sms, Plan& pl) {
   const long long per = (nt + clu - 1) / clu;   // units per CTA
   if ((clu - 1) * per >= nt) return;            // every rank has units
   const long long off = (static_cast<long long>(pl.smem) - 1024 + 15) & ~15ll;
-  const long long bytes = static_cast<long long>(pl.slot_cols) * (pl.D + 4) * 4;
+  // rank 0's arrival barrier (16 B), then every CTA's piece rows
+  const long long bytes = 16 + static_cast<long long>(clu) * pl.slot_cols * (pl.D + 4) * 4;
   if (off + bytes + 1024 > kMaxSmem) return;
   Plan c = pl;
   c.clu = clu;
