@@ -1052,10 +1052,13 @@ __global__ void __launch_bounds__(NW * 32, 1)
                                                   p.div_ng)),
                         p.gsz);
       set_ranges(U, P, p.gsz == 1 ? P : (P + NW - 1) / NW);
-      if (p.snap && P >= 2 * p.max_nt) {
+      if (p.snap && P >= 8 * p.max_nt) {
         // Both CTAs that share a boundary compute the same snapped value; a
         // boundary moves by at most half a segment (< P / 2), so the groups
-        // stay ordered and every segment lies inside one group.
+        // stay ordered and every segment lies inside one group. Only while a
+        // move costs a CTA at most 1/16 of its share: B96 S<=256 Hq32/Hkv16
+        // (47 tiles per CTA, segments up to 8) was 2 us slower snapped, B128
+        // S<=256 MHA (235 tiles per CTA, segments up to 16) 0.9 us faster.
         const int nseg = p.Hkv * p.QC;
         auto snap = [&](long long at) -> int {
           if (at >= U) return U;
