@@ -69,10 +69,15 @@ def _cases():
         ("gqa8_bf16_b1_s8192_merge_pass", workloads.build(
             "noalloc_long", 1, 64, 8, 16, torch.bfloat16, 8192, 512, 512, seed=35,
             device="cuda"), 0),
+        # one 4096-token sequence over 32 heads with pages of 128 tokens: the
+        # thread-block cluster schedule (no scratch partials beyond counters)
+        ("mha_bf16_b1_s4096_cluster", workloads.build(
+            "noalloc_cluster", 1, 32, 32, 128, torch.bfloat16, 4096, 32, 40, seed=37,
+            device="cuda"), 0),
     ]
 
 
-@pytest.mark.parametrize("case", range(4))
+@pytest.mark.parametrize("case", range(5))
 def test_noalloc_matches_pa_decode_on_two_calls(case):
     import oracle
     import paged_attention as pa
@@ -82,6 +87,8 @@ def test_noalloc_matches_pa_decode_on_two_calls(case):
                           ns or None)
     if name.endswith("merge_pass"):
         assert plan["merge_pass"] == 1 and plan["group_warps"] == 1, plan
+    if name.endswith("_cluster"):
+        assert plan["cluster_size"] >= 2, plan
     assert plan["workspace_bytes"] + 4 * plan["counter_count"] <= \
         _native.PA_NOALLOC_SCRATCH_BYTES, plan
     # the existing entry point (caller-provided workspace)
