@@ -2341,14 +2341,18 @@ static pa_status_t validate_launch(const pa_decode_params* p) {
 // with L2 flushed; B4 S8192 page 64: 94.6 -> 89.2 us); 2- or 4-head groups as
 // 32-token tiles on 6 warps. head_dim 64 (128-byte rows):
 // MHA as 32-token tiles on 6 warps, query-head groups as 64-token tiles on 6
-// warps. head_dim 256: MHA as 16-token tiles on 5 warps, groups as 32-token
-// tiles on 3 warps.
+// warps. head_dim 256: MHA and pairs as 16-token tiles on 5 warps, groups of
+// 4 as 16-token tiles on 4 warps, wider groups as 32-token tiles on 3 warps.
 static int pick_variant(const pa_decode_params* p, bool dup) {
   int v = p->kernel_variant;
   if (v == 0) {
     const int g = p->num_heads / p->num_kv_heads;
     if (p->head_dim == 256)
-      v = g == 1 ? 7 : 9;   // MHA: 16-token tiles on 5 warps; groups: 32-token tiles on 3
+      // MHA and pairs: 16-token tiles on 5 warps; groups of 4: 16-token tiles
+      // on 4 warps, whose merge rows for 4 columns fit in shared memory (B32
+      // S1024 Hq32/Hkv8: 57.7 us against 60.1 on 32x3x2); wider groups:
+      // 32-token tiles on 3 warps
+      v = (g == 1 || g == 2) ? 7 : (g == 4 ? 6 : 9);
     else if (p->head_dim == 64)
       v = g == 1 ? 3 : 8;   // MHA: 32-token tiles on 6 warps; groups: 64-token tiles
     else
