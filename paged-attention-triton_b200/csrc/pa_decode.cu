@@ -2343,7 +2343,7 @@ static pa_status_t validate_launch(const pa_decode_params* p) {
 // MHA as 32-token tiles on 6 warps, query-head groups as 64-token tiles on 6
 // warps. head_dim 256: MHA and pairs as 16-token tiles on 5 warps, groups of
 // 4 as 16-token tiles on 4 warps, wider groups as 32-token tiles on 3 warps.
-static int pick_variant(const pa_decode_params* p, bool dup) {
+static int pick_variant(const pa_decode_params* p, bool dup, int sms) {
   int v = p->kernel_variant;
   if (v == 0) {
     const int g = p->num_heads / p->num_kv_heads;
@@ -2357,14 +2357,26 @@ static int pick_variant(const pa_decode_params* p, bool dup) {
       v = g == 1 ? 3 : 8;   // MHA: 32-token tiles on 6 warps; groups: 64-token tiles
     else
       v = (!dup || g == 1) ? 5 : 3;
-    // 32x6x2 keeps its warps' merge rows in shared memory only up to 2 query
-    // columns; with more, and segments that can exceed 8 tiles, 16x8x2 (whose
-    // merge rows fit) wins over merging through the workspace.
-    if (v == 3 && p->head_dim == 128) {
+    // Query-head groups whose segments can exceed 8 tiles of 32 tokens. 32x6x2
+    // keeps its warps' merge rows in shared memory only up to 2 query columns.
+    // With more columns: no more segments than SMs -> 32x6x2 as single-warp
+    // groups whose pieces meet in the merge pass (B1 S4096 Hq32/Hkv8 15.4 us
+    // against 19.5 on 16x8x2, B16 S1024 25.6 against 27.8, B1 S32768
+    // Hq32/Hkv4 25.8 against 27.8), except same-length rows of >= 8192 tokens
+    // that the cluster schedule covers on 16x8x2 (B8 S32768: 170.7 against
+    // 174.7); more segments than SMs -> 16x8x2, whose merge rows fit (B64 S512:
+    // 37.0 against 40.3 with 32x6x2's rows in the workspace).
+    if (p->head_dim == 128 && g > 1) {
+      const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
+      const long long nseg = static_cast<long long>(p->batch) * p->num_kv_heads * ((g + 7) / 8);
       const int cols = std::min(g, 8);
       const bool fits = variant_smem_base(3, dup, 128) + 6 * 2 * (128 + 4) * 4 * cols <= kMaxSmem;
-      const long long cap = static_cast<long long>(p->max_blocks) * p->block_size;
-      if (!fits && (cap + 31) / 32 > 8) v = 5;
+      if (!fits && (cap + 31) / 32 > 8) {
+        const long long clu = nseg > 0 ? std::min<long long>(8, sms / nseg) : 0;
+        const bool clusters = p->seq_lens == nullptr && p->seq_len >= 8192 && clu >= 2 &&
+                              4 * nseg * clu >= 3ll * sms;
+        v = (nseg <= sms && !clusters) ? 3 : 5;
+      }
     }
   }
   if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
@@ -2464,7 +2476,7 @@ static pa_status_t make_plan(const pa_decode_params* p, int sms, Plan& pl,
     pl.counters = 0;
     return PA_OK;
   }
-  pl.variant = pick_variant(p, pl.dup);
+  pl.variant = pick_variant(p, pl.dup, sms);
   if (pl.variant == 0) return PA_ERR_UNSUPPORTED;
   const Variant& v = kVariants[pl.variant - 1];
   const long long nseg = static_cast<long long>(p->num_kv_heads) * pl.QC;
