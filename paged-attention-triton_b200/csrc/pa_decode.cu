@@ -2928,14 +2928,19 @@ static void build_kparams(const pa_decode_params* p, const Plan& pl, KParams& kp
     kp.per_row = p->num_kv_heads * pl.QC * kp.nt_u;
     kp.U = p->batch * kp.per_row;            // fits int32: checked by make_plan
     kp.P = std::max((kp.U + ngroups - 1) / ngroups, pl.gsz);
-    // Whole segments per group when that costs at most 3 % of balance: no
-    // segment then crosses a group, so no piece needs the global merge (its
-    // fence, atomic and extra round trip land on one warp of the group and
-    // make that warp the group's last).
+    // Whole segments per group when that costs at most 25 % more units in the
+    // fullest group (40 % with query-head groups, whose split segments would
+    // otherwise go through the merge pass): no segment then crosses a group,
+    // so no piece needs a cross-CTA merge, whose round trips land on the tail
+    // of the step. Same-length steps, L2 flushed: B32 S1024 MHA at D = 256
+    // (+16 %, 128 CTAs) 91.4 -> 86.4 us, B12 S1024 H32 41.5 -> 39.1, B40 S1024
+    // Hq32/Hkv8 (+39 %) 43.5 -> 39.2; B10 S2048 H32 (+39 %) 60.6 -> 61.9 and
+    // B5 S4096 H32 (+85 %, 80 CTAs) 61.6 -> 78.1 stay unaligned.
     const long long nseg_total = static_cast<long long>(p->batch) * p->num_kv_heads * pl.QC;
     if (kp.nt_u > 0 && nseg_total >= ngroups) {
       const long long aligned = (nseg_total + ngroups - 1) / ngroups * kp.nt_u;
-      if (aligned * 100 <= static_cast<long long>(kp.P) * 103 && aligned >= pl.gsz)
+      const long long limit = pl.slot_cols > 1 ? 140 : 125;
+      if (aligned * 100 <= static_cast<long long>(kp.P) * limit && aligned >= pl.gsz)
         kp.P = static_cast<int>(aligned);
     }
     kp.Pw = (kp.P + pl.gsz - 1) / pl.gsz;
