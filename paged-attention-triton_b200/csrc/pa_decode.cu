@@ -2377,6 +2377,14 @@ static int pick_variant(const pa_decode_params* p, bool dup, int sms) {
                               4 * nseg * clu >= 3ll * sms;
         v = (nseg <= sms && !clusters) ? 3 : 5;
       }
+      // 16x8x2 without duplicated columns holds the merge rows of at most 7
+      // query columns; with 8 and more segments than SMs they would go to the
+      // workspace, so 32x4x2, whose rows fit, takes over (the C5 shards of 8
+      // ranks, B256 Hq8/Hkv1: 187.5 -> 155.9 us; of 4 ranks 316 -> 287;
+      // B128 S<=1024 Hq64/Hkv8 79.8 -> 61.5 us flushed).
+      if (v == 5 && !dup && nseg > sms && (cap + 15) / 16 > 8 &&
+          variant_smem_base(5, false, 128) + 8 * 2 * (128 + 4) * 4 * cols > kMaxSmem)
+        v = 10;
     }
   }
   if (p->head_dim == 128 && !dup && (v == 2 || v == 4)) v = 5;
